@@ -1,0 +1,306 @@
+"""Benchmark: paged-attention decode tokens/s (+ HBM GB/s) on B200.
+
+One step = append one token per sequence through the slot mapping, then decode
+every sequence over ctx+1 tokens (one call of the fused C-ABI entry point).
+Default workload: configuration c2 (Llama-7B-shaped, f32 KV, batch 64, 32
+heads x 128, block 16, context 2048, 16384-block pool).  Under torchrun each
+rank runs its own full c2 workload (weak scaling; sequences are independent,
+no data-path collective).  Inputs (4.3 GB of KV per rank) exceed the 126 MB
+L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2]
+  python bench.py --impl reference ...   # CPU arm (the oracle port)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged-attn decode tokens/s"
+
+
+def _peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index: int):
+        self.index, self.samples, self.reasons, self.stop = index, [], set(), threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+        self.t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self.stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.05)
+
+    def __enter__(self):
+        if self.nv:
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop.set()
+        if self.nv:
+            self.t.join()
+
+    def summary(self) -> dict:
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def host_sample_case(spec, n_seqs: int, seed: int = 1):
+    """A CPU-side case with the shapes and value distributions of `spec` for
+    `n_seqs` sequences (a pool of exactly the blocks they use)."""
+    import numpy as np
+    from dataclasses import replace
+
+    import torch
+
+    from clove_b200.workload import fill_values, make_layout, to_numpy_bits
+    lay = make_layout(replace(spec, num_blocks=0, tables="permutation"), seed=spec.seed + seed, batch=n_seqs)
+    q, _, _, st = fill_values(lay, "cpu")
+    bits = to_numpy_bits(st)
+    return lay, (np.ascontiguousarray(bits[0]), np.ascontiguousarray(bits[1]), lay.block_tables,
+                 (lay.context_lens + 1).astype(np.int32), to_numpy_bits(q))
+
+
+def cpu_arm(lay, case, budget_s: float, max_reps: int | None = None) -> dict:
+    """Time the oracle's f32 restatement (reference CPU idiom) on the host
+    cores over the sampled sequences, repeated for about `budget_s` seconds."""
+    import numpy as np
+
+    import oracle
+    from clove_b200.workload import dtype_code
+    kc, vc, bt, ctx, qs = case
+    threads = os.cpu_count() or 1
+    code = dtype_code(lay.spec.dtype)
+    scale = 1.0 / np.sqrt(lay.spec.head_dim)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.decode_f32(code, qs, kc, vc, bt, ctx, scale, nthreads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or (max_reps and reps >= max_reps):
+            break
+    seqs = ctx.shape[0]
+    return {"value": seqs * reps / el, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{seqs} sequences shaped like config {lay.spec.name} (ctx+1 = "
+                      f"{int(ctx.min())}..{int(ctx.max())}), decode only, {reps} reps in {el:.1f} s"}
+
+
+def _dist():
+    import torch
+    import torch.distributed as dist
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1 and not dist.is_initialized():
+        torch.cuda.set_device(local) if torch.cuda.is_available() else None
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo")
+    return ws, rank, local
+
+
+def run_reference(args) -> None:
+    """CPU arm: the oracle port of the reference's CPU idiom on the host cores,
+    a bounded sample of the workload per step; rank 0 only."""
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    from clove_b200.workload import CONFIGS
+    spec = CONFIGS[args.config]
+    n = args.cpu_seqs
+    lay, case = host_sample_case(spec, n)
+    for _ in range(args.warmup):
+        cpu_arm(lay, case, 0.0, max_reps=1)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_arm(lay, case, 0.0, max_reps=1)
+    el = time.perf_counter() - t0
+    val = n * args.steps / el
+    cb = {"value": val, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+          "sample": f"per step {n} sequences shaped like config {spec.name} (ctx+1 = "
+                    f"{int(case[3].min())}..{int(case[3].max())}), oracle f32 restatement, all host threads"}
+    print(json.dumps({"metric": METRIC, "value": val, "unit": "tokens/s", "impl": "reference", "n_gpus": ws,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": _dtype_name(spec.dtype),
+                      "data": "synthetic", "config": {"workload": spec.name, "batch_per_step": n},
+                      "cpu_baseline": cb,
+                      "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def _dtype_name(dt) -> str:
+    import torch
+    return {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16"}[dt]
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from clove_b200 import KVPool, launch_count
+    from clove_b200.workload import CONFIGS, fill_values, make_layout
+
+    ws, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    spec = CONFIGS[args.config]
+    lay = make_layout(spec, seed=spec.seed + rank)  # weak scaling: one full workload per rank
+    pool = KVPool(lay.num_blocks, spec.block_size, spec.num_kv_heads, spec.head_dim, spec.dtype, dev)
+    q, kn, vn, _ = fill_values(lay, dev, pool.storage)
+    bt = torch.from_numpy(lay.block_tables).to(dev)
+    cl = torch.from_numpy(lay.context_lens).to(dev)
+    out = torch.empty((lay.batch, spec.num_q_heads, spec.head_dim), dtype=torch.float32, device=dev)
+    max_ctx = lay.max_ctx
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        pool.append_decode(q, kn, vn, bt, cl, max_ctx=max_ctx, out=out, stream=stream)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if pool.decode_status(lay.batch, spec.num_q_heads, max_ctx) != 0:
+        raise RuntimeError("device check flags raised on the bench workload")
+
+    # ---- device-timed region: inputs resident in HBM ----
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    n0 = launch_count()
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    launches = launch_count() - n0
+    ms = ev0.elapsed_time(ev1) / args.steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # ---- end to end: host (pinned) inputs -> device -> result back to host ----
+    hq = q.cpu().pin_memory()
+    hk, hv = kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    hbt, hcl = bt.cpu().pin_memory(), cl.cpu().pin_memory()
+    hout = torch.empty(out.shape, dtype=torch.float32).pin_memory()
+    dq, dk, dv, dbt, dcl = (torch.empty_like(x, device=dev) for x in (hq, hk, hv, hbt, hcl))
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hbt, hcl))
+    d2h = hout.numel() * 4
+
+    def e2e_step():
+        for d, h in ((dq, hq), (dk, hk), (dv, hv), (dbt, hbt), (dcl, hcl)):
+            d.copy_(h, non_blocking=True)
+        pool.append_decode(dq, dk, dv, dbt, dcl, max_ctx=max_ctx, out=out, stream=stream)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+
+    if rank != 0:
+        return
+    tokens = lay.batch * ws
+    kv_bytes = lay.kv_bytes()  # per rank per step
+    achieved = kv_bytes / (ms * 1e-3) / 1e9
+    peak, peak_kind = _peaks()
+    _, case = host_sample_case(spec, args.cpu_seqs)
+    cb = cpu_arm(lay, case, args.cpu_seconds)
+    line = {
+        "metric": METRIC, "value": tokens / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": _dtype_name(spec.dtype), "data": "synthetic",
+        "config": {"workload": spec.name, "description": spec.description, "batch_per_gpu": lay.batch,
+                   "global_batch": tokens, "num_q_heads": spec.num_q_heads, "num_kv_heads": spec.num_kv_heads,
+                   "head_dim": spec.head_dim, "block_size": spec.block_size, "num_blocks": lay.num_blocks,
+                   "kv_bytes_per_gpu_step": kv_bytes, "l2": "inputs larger than L2 (no flush)",
+                   "parallelism": f"dp{ws} (independent sequences per GPU)"},
+        "hbm_gbs": achieved,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": args.traffic,
+                     "note": f"KV bytes per step / whole step time (plan + decode kernels), peak {peak_kind}"},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "cpu_baseline": cb,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2")
+    ap.add_argument("--cpu-seqs", type=int, default=8)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="dram bytes per decode launch from an ncu capture (reported as roofline.traffic)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+    try:
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,96 @@
+"""Python mirror of the reference's PagedAttention interface on the CUDA path.
+
+  CudaBackend.paged_attention(q, k, v, kv_cache, block_tables, context_lens)
+      <- Backend::paged_attention, src/backend.rs:249-256
+  PagedAttention(dim, num_heads).forward(x, kv_cache, block_tables, context_lens)
+      <- PagedAttention::forward, src/nn.rs:531-546
+
+Tensors are torch CUDA tensors.  kv_cache is ONE tensor
+[2, num_blocks, block_size, num_kv_heads, head_dim] (K plane, V plane): the
+reference passes a single kv_cache and documents the per-plane layout at
+src/nn.rs:534.  q: [B, Hq*D]; k, v: [B, Hkv*D] — the new token's projections;
+context_lens: int32 [B] lengths before this token.  The call appends k, v
+through the slot mapping and attends over ctx + 1 tokens; it returns f32
+[B, Hq*D] (the reference output dtype, src/lazy.rs:5252).  context_lens is
+not modified; the caller advances it.
+
+Errors raise CloveError (the reference panics, src/backend.rs:2937-2948).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .ops import KVPool
+
+
+class CudaBackend:
+    """Stateless apart from a cache of pool handles keyed by kv_cache storage."""
+
+    _pools: dict[tuple[int, tuple, torch.dtype], KVPool] = {}
+
+    @classmethod
+    def _pool(cls, kv_cache: torch.Tensor) -> KVPool:
+        if kv_cache.dim() != 5 or kv_cache.shape[0] != 2:
+            raise ValueError("kv_cache must be [2, num_blocks, block_size, num_kv_heads, head_dim]")
+        key = (kv_cache.data_ptr(), tuple(kv_cache.shape), kv_cache.dtype)
+        pool = cls._pools.get(key)
+        if pool is None:
+            _, nb, bs, hkv, d = kv_cache.shape
+            pool = KVPool(nb, bs, hkv, d, dtype=kv_cache.dtype, device=kv_cache.device, storage=kv_cache)
+            cls._pools[key] = pool
+        return pool
+
+    @classmethod
+    def paged_attention(cls, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_cache: torch.Tensor,
+                        block_tables: torch.Tensor, context_lens: torch.Tensor,
+                        max_ctx: int | None = None) -> torch.Tensor:
+        pool = cls._pool(kv_cache)
+        B = context_lens.numel()
+        out = pool.append_decode(q.contiguous(), k.contiguous(), v.contiguous(), block_tables, context_lens,
+                                 scale=1.0 / math.sqrt(pool.head_dim), max_ctx=max_ctx)
+        return out.reshape(B, -1)
+
+
+class Linear:
+    """y = x W + b with W [in, out] (the reference Linear, src/nn.rs:102-123).
+    A plain library GEMM: the projections are not part of the decode path."""
+
+    def __init__(self, in_dim: int, out_dim: int, device, dtype=torch.float32, generator=None):
+        bound = 1.0 / math.sqrt(in_dim)
+        self.weight = (torch.rand((in_dim, out_dim), generator=generator, device=device) * 2 - 1).mul_(bound) \
+            .to(dtype)
+        self.bias = torch.zeros(out_dim, device=device, dtype=dtype)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return torch.addmm(self.bias, x, self.weight)
+
+
+class PagedAttention:
+    """PagedAttention::new(dim, num_heads) (src/nn.rs:543-553) with the KV-head
+    count added for GQA: w_k/w_v project to num_kv_heads*head_dim."""
+
+    def __init__(self, dim: int, num_heads: int, num_kv_heads: int | None = None, device="cuda",
+                 dtype=torch.float32, seed: int = 0):
+        self.num_heads = num_heads
+        self.num_kv_heads = num_kv_heads or num_heads
+        self.head_dim = dim // num_heads
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        kv_dim = self.num_kv_heads * self.head_dim
+        self.w_q = Linear(dim, dim, device, dtype, g)
+        self.w_k = Linear(dim, kv_dim, device, dtype, g)
+        self.w_v = Linear(dim, kv_dim, device, dtype, g)
+        self.w_o = Linear(dim, dim, device, torch.float32, g)
+
+    def forward(self, x: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
+                context_lens: torch.Tensor, max_ctx: int | None = None) -> torch.Tensor:
+        q = self.w_q.forward(x)
+        k = self.w_k.forward(x)
+        v = self.w_v.forward(x)
+        attn = CudaBackend.paged_attention(q, k, v, kv_cache, block_tables, context_lens, max_ctx=max_ctx)
+        return self.w_o.forward(attn)
+
+    def parameters(self) -> list[torch.Tensor]:
+        return [t for l in (self.w_q, self.w_k, self.w_v, self.w_o) for t in (l.weight, l.bias)]

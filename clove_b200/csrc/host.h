@@ -1,0 +1,74 @@
+// Host-side declarations shared by the C-ABI layer and the kernel launchers.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/clove_cuda.h"
+
+// The pool handle behind clove_pool_t.
+struct clove_pool {
+  int device;
+  int num_blocks;
+  int block_size;
+  int num_kv_heads;
+  int head_dim;
+  int dtype;
+  int elem_bytes;
+  int owns_memory;
+  void* k_cache;
+  void* v_cache;
+  size_t plane_bytes;
+  int32_t* flags;   // device word for the append / gather kernels' check flags
+  int num_sms;
+  CUtensorMap tm_k;  // 3-D maps {head_dim, num_kv_heads, num_blocks*block_size}
+  CUtensorMap tm_v;
+};
+
+namespace clove {
+
+// Workspace carve-up for one decode call; offsets in bytes from the base.
+struct DecodeLayout {
+  int chunk_blocks;
+  int max_chunks;
+  size_t off_err, off_nitems, off_items, off_seq_chunks, off_counters, off_partials;
+  size_t total;
+};
+
+DecodeLayout decode_layout(const clove_pool& pool, int batch, int num_q_heads, int max_ctx);
+
+struct DecodeCall {
+  const void* q;
+  const void* k_new;  // null: plain decode
+  const void* v_new;
+  int num_q_heads;
+  const int32_t* block_tables;
+  int bt_stride;
+  const int32_t* context_lens;
+  int batch;
+  float scale;
+  int max_ctx;
+  float* out;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+// Returns a CLOVE_* status; sets the thread's last-error text on failure.
+int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t stream);
+
+cudaError_t launch_reshape_and_cache(const void* k, const void* v, void* k_cache, void* v_cache,
+                                     const int32_t* slot_mapping, int num_tokens, int row_bytes,
+                                     long long num_slots, int32_t* flags, cudaStream_t stream);
+cudaError_t launch_gather_kv(const void* k_cache, const void* v_cache, const int32_t* block_tables,
+                             int bt_stride, const int32_t* context_lens, int batch, int max_ctx,
+                             int block_size, int num_blocks, int row_bytes, void* k_out, void* v_out,
+                             int32_t* flags, cudaStream_t stream);
+
+// error text / launch accounting (capi.cu)
+void set_last_error(const char* fmt, ...);
+void count_launches(int n);
+int decode_variant();  // 0 auto, 1 simt, 2 mma
+
+}  // namespace clove

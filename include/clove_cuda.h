@@ -1,0 +1,186 @@
+/*
+ * clove_cuda.h — C ABI of the B200-native PagedAttention decode library
+ * (libclove_cuda.so, built for sm_100a).
+ *
+ * The reference (rakeshpdey/clove, Rust) exposes the hot path as
+ *   Backend::paged_attention(q, k, v, kv_cache, block_tables, context_lens)
+ *     src/backend.rs:249-256
+ *   PagedAttention::forward(x, kv_cache, block_tables, context_lens)
+ *     src/nn.rs:531-546
+ *   clove_paged_attention(q, k, v, kv, bt, cl) -> CTensor
+ *     src/ffi.rs:247-266
+ * and has no working implementation of it (the eager backend panics at
+ * src/backend.rs:2937-2948; the lazy WGSL kernel at src/lazy.rs:5243-5275 is a
+ * placeholder).  The entry points below are what a Rust `CudaBackend`
+ * declares in an `extern "C"` block to replace those three.
+ *
+ * Conventions
+ *   - Every function returns an int status (CLOVE_OK == 0, negative on
+ *     error) and never aborts; clove_cuda_get_last_error() gives the text.
+ *   - All tensor pointers are device pointers on the pool's device unless a
+ *     function says otherwise.  Calls are asynchronous on `stream`
+ *     (a cudaStream_t; NULL = legacy default stream).
+ *   - KV cache layout (per plane, K and V):  [num_blocks, block_size,
+ *     num_kv_heads, head_dim], row-major — the layout documented at
+ *     src/nn.rs:534 with the KV-head count made explicit for GQA.
+ *   - block_tables: int32 [batch, bt_stride] (src/nn.rs:535; the reference
+ *     hardcodes a stride of 1024 at src/lazy.rs:5264, here it is a parameter).
+ *   - context_lens: int32 [batch] (src/nn.rs:536).
+ *   - q: [batch, num_q_heads, head_dim] in the pool dtype; out: float32
+ *     [batch, num_q_heads, head_dim] (the reference output is f32,
+ *     src/lazy.rs:5252).  Query head hq reads KV head hq / (num_q_heads /
+ *     num_kv_heads).
+ *   - Scale: the caller passes it; the reference uses 1/sqrt(head_dim)
+ *     (src/lazy.rs:5267, src/nn/attention.rs:64).
+ */
+#ifndef CLOVE_CUDA_H
+#define CLOVE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define CLOVE_OK                 0
+#define CLOVE_ERR_INVALID_ARG   -1  /* bad shape, null pointer, misalignment   */
+#define CLOVE_ERR_UNSUPPORTED   -2  /* head_dim / group / dtype not built       */
+#define CLOVE_ERR_CUDA          -3  /* a CUDA runtime call failed               */
+#define CLOVE_ERR_OOM           -4  /* device allocation failed (pool create)   */
+#define CLOVE_ERR_WORKSPACE     -5  /* workspace too small                      */
+#define CLOVE_ERR_DEVICE_CHECK  -6  /* a kernel flagged bad indices (see flags) */
+#define CLOVE_ERR_NO_DEVICE     -7  /* no CUDA device / ordinal out of range    */
+
+/* ---- device-side check flags, reported by clove_cuda_decode_status ------ */
+#define CLOVE_FLAG_BLOCK_OOB     1  /* a block-table entry outside [0, num_blocks) */
+#define CLOVE_FLAG_CTX_RANGE     2  /* a context length < 0 or > max_ctx          */
+#define CLOVE_FLAG_SLOT_OOB      4  /* a slot_mapping entry >= num_blocks*block_size */
+#define CLOVE_FLAG_TIMEOUT       8  /* a bounded pipeline wait ran out            */
+
+/* ---- dtypes: the reference's FFI precision codes (src/ffi.rs:305-313) ---- */
+#define CLOVE_DTYPE_F32    0
+#define CLOVE_DTYPE_F16   16
+#define CLOVE_DTYPE_BF16 160
+
+typedef struct clove_pool* clove_pool_t;
+
+typedef struct clove_pool_info {
+    int device;
+    int num_blocks;
+    int block_size;
+    int num_kv_heads;
+    int head_dim;
+    int dtype;
+    int owns_memory;      /* 1: created by pool_create, 0: wrapped */
+    void* k_cache;        /* device pointer, plane K */
+    void* v_cache;        /* device pointer, plane V */
+    size_t plane_bytes;   /* bytes of one plane */
+} clove_pool_info_t;
+
+/* Number of visible CUDA devices (replaces the adapter enumeration of
+ * EngineDevice::init, src/device.rs:79-150, and MultiGPUOrchestrator::new,
+ * src/distributed.rs:58-120). */
+int clove_cuda_init(int* num_devices);
+
+/* Last error text of the calling thread (empty string if none). */
+int clove_cuda_get_last_error(char* buf, size_t n);
+
+/* Device-resident KV block pool: one allocation [2, num_blocks, block_size,
+ * num_kv_heads, head_dim] (K plane then V plane), owned by the handle.
+ * The reference passes a caller-made kv_cache tensor (src/nn.rs:534) and has
+ * no allocator; its only pool is the size-keyed BufferPool
+ * (src/device.rs:177-222). */
+int clove_cuda_pool_create(int device, int num_blocks, int block_size,
+                           int num_kv_heads, int head_dim, int dtype,
+                           clove_pool_t* out);
+
+/* Wrap caller-owned K and V planes (each [num_blocks, block_size,
+ * num_kv_heads, head_dim], 16-byte aligned) without taking ownership. */
+int clove_cuda_pool_wrap(int device, void* k_cache, void* v_cache,
+                         int num_blocks, int block_size, int num_kv_heads,
+                         int head_dim, int dtype, clove_pool_t* out);
+
+int clove_cuda_pool_destroy(clove_pool_t pool);
+
+/* Synchronise `stream`, read and clear the check flags that the append and
+ * gather kernels of this pool raised since the last call (CLOVE_FLAG_*). */
+int clove_cuda_pool_status(clove_pool_t pool, void* stream, int* flags);
+int clove_cuda_pool_info(clove_pool_t pool, clove_pool_info_t* info);
+
+/* KV append (reshape-and-cache): for each token i with slot s =
+ * slot_mapping[i] >= 0, copy k[i, :, :] -> K[s / block_size, s % block_size]
+ * and v[i] -> V[...], bit for bit.  k, v: [num_tokens, num_kv_heads,
+ * head_dim] in the pool dtype.  Negative slots are skipped (padding).  The
+ * reference passes the new k, v to paged_attention (src/nn.rs:539-543,
+ * src/lazy.rs:5247-5248) but never writes them to the cache. */
+int clove_cuda_reshape_and_cache(clove_pool_t pool, const void* k,
+                                 const void* v, const int32_t* slot_mapping,
+                                 int num_tokens, void* stream);
+
+/* Block-table gather (debug / parity): k_out, v_out: [batch, max_ctx,
+ * num_kv_heads, head_dim] in the pool dtype; token t of sequence b is read
+ * from physical block block_tables[b*bt_stride + t/block_size], offset
+ * t % block_size — the indexing of src/lazy.rs:5259-5270 with explicit heads
+ * and table stride.  Rows t >= context_lens[b] are zero-filled. */
+int clove_cuda_gather_kv(clove_pool_t pool, const int32_t* block_tables,
+                         int bt_stride, const int32_t* context_lens,
+                         int batch, int max_ctx, void* k_out, void* v_out,
+                         void* stream);
+
+/* Bytes of scratch workspace paged_decode / paged_append_decode need for
+ * this batch, head count and maximum context length (tokens attended,
+ * i.e. including the appended token). */
+size_t clove_cuda_decode_workspace_size(clove_pool_t pool, int batch,
+                                        int num_q_heads, int max_ctx);
+
+/* Decode: for every sequence b and query head hq,
+ *   out[b,hq,:] = softmax_t(scale * <q[b,hq,:], K_t>) . V_t
+ * over the context_lens[b] cached tokens of sequence b (semantics of
+ * src/nn/attention.rs:52-69; gather of src/lazy.rs:5259-5270).  A sequence
+ * with context length 0 gets a zero output row.  `workspace` (device memory,
+ * >= clove_cuda_decode_workspace_size bytes, 256-byte aligned) is scratch;
+ * the call allocates nothing. */
+int clove_cuda_paged_decode(clove_pool_t pool, const void* q, int num_q_heads,
+                            const int32_t* block_tables, int bt_stride,
+                            const int32_t* context_lens, int batch,
+                            float scale, int max_ctx, float* out,
+                            void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* Append + decode in one launch (the CudaBackend body of
+ * Backend::paged_attention, src/backend.rs:249-256): context_lens holds the
+ * lengths BEFORE this step; k_new, v_new: [batch, num_kv_heads, head_dim] are
+ * written to slot block_tables[b][ctx_b / block_size]*block_size +
+ * ctx_b % block_size, then the sequence attends over ctx_b + 1 tokens.
+ * context_lens is not modified (the caller advances it). */
+int clove_cuda_paged_append_decode(clove_pool_t pool, const void* q,
+                                   const void* k_new, const void* v_new,
+                                   int num_q_heads,
+                                   const int32_t* block_tables, int bt_stride,
+                                   const int32_t* context_lens, int batch,
+                                   float scale, int max_ctx, float* out,
+                                   void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
+/* Synchronise `stream` and read the device check flags (CLOVE_FLAG_*) that
+ * the most recent decode call on `workspace` raised (each call clears them
+ * when it starts); the word is cleared after reading.  Returns
+ * CLOVE_ERR_DEVICE_CHECK if any flag was set, CLOVE_OK otherwise. */
+int clove_cuda_decode_status(void* workspace, void* stream, int* flags);
+
+/* Kernel-variant selection for decode: 0 = automatic (default), 1 = force
+ * the CUDA-core kernel, 2 = force the tensor-core kernel (bf16/f16 with
+ * group >= 4 only).  Process-wide; for tests and measurement. */
+int clove_cuda_set_decode_variant(int variant);
+
+/* Number of kernels the library launched since load (for the bench's
+ * launch count). */
+uint64_t clove_cuda_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CLOVE_CUDA_H */

@@ -1,0 +1,108 @@
+"""Error behaviour on the GPU: bad inputs give status codes or device check
+flags, never a fault (out-of-range indices are clamped and flagged)."""
+import numpy as np
+import pytest
+import torch
+
+from clove_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(dtype=torch.float32):
+    from clove_b200 import KVPool
+    pool = KVPool(64, 16, 2, 128, dtype=dtype, device=0)
+    pool.storage.normal_()
+    dev = torch.device("cuda", 0)
+    bt = torch.arange(8, dtype=torch.int32, device=dev).reshape(2, 4)
+    cl = torch.tensor([20, 40], dtype=torch.int32, device=dev)
+    q = torch.randn(2, 4, 128, device=dev).to(dtype)
+    return pool, bt, cl, q
+
+
+def test_bad_block_id_flagged():
+    pool, bt, cl, q = _setup()
+    bt[1, 1] = 10 ** 6
+    pool.decode(q, bt, cl, max_ctx=64)
+    assert pool.decode_status(2, 4, 64) & _lib.FLAG_BLOCK_OOB
+    bt[1, 1] = -3
+    pool.decode(q, bt, cl, max_ctx=64)
+    assert pool.decode_status(2, 4, 64) & _lib.FLAG_BLOCK_OOB
+
+
+def test_context_over_max_ctx_flagged_and_clamped():
+    pool, bt, cl, q = _setup()
+    out = pool.decode(q, bt, cl, max_ctx=30)
+    assert pool.decode_status(2, 4, 30) & _lib.FLAG_CTX_RANGE
+    assert torch.isfinite(out).all()
+    cl[0] = -5
+    out = pool.decode(q, bt, cl, max_ctx=64)
+    assert pool.decode_status(2, 4, 64) & _lib.FLAG_CTX_RANGE
+    assert (out[0] == 0).all()
+
+
+def test_clean_call_clears_flags():
+    pool, bt, cl, q = _setup()
+    bt2 = bt.clone()
+    bt2[0, 0] = 999
+    pool.decode(q, bt2, cl, max_ctx=64)
+    pool.decode(q, bt, cl, max_ctx=64)
+    assert pool.decode_status(2, 4, 64) == 0
+
+
+def test_slot_oob_flagged_by_append():
+    pool, *_ = _setup()
+    dev = torch.device("cuda", 0)
+    k = torch.randn(3, 2, 128, device=dev)
+    pool.reshape_and_cache(k, k, torch.tensor([0, 64 * 16, -1], dtype=torch.int32, device=dev))
+    assert pool.pool_status() & _lib.FLAG_SLOT_OOB
+    assert pool.pool_status() == 0  # read clears
+
+
+def test_host_validation_codes():
+    import ctypes as C
+    pool, bt, cl, q = _setup()
+    L = _lib.lib()
+    out = torch.empty(2, 4, 128, device="cuda")
+    ws = pool.workspace(2, 4, 64)
+    # workspace too small
+    rc = L.clove_cuda_paged_decode(pool.handle, q.data_ptr(), 4, bt.data_ptr(), 4, cl.data_ptr(), 2, 0.1, 64,
+                                   out.data_ptr(), ws.data_ptr(), 8, None)
+    assert rc == _lib.ERR_WORKSPACE
+    # q heads not a multiple of kv heads
+    rc = L.clove_cuda_paged_decode(pool.handle, q.data_ptr(), 3, bt.data_ptr(), 4, cl.data_ptr(), 2, 0.1, 64,
+                                   out.data_ptr(), ws.data_ptr(), ws.numel(), None)
+    assert rc == _lib.ERR_INVALID_ARG
+    # max_ctx beyond the table capacity
+    rc = L.clove_cuda_paged_decode(pool.handle, q.data_ptr(), 4, bt.data_ptr(), 4, cl.data_ptr(), 2, 0.1, 65,
+                                   out.data_ptr(), ws.data_ptr(), ws.numel(), None)
+    assert rc == _lib.ERR_INVALID_ARG
+    # unsupported head_dim
+    h = C.c_void_p()
+    assert L.clove_cuda_pool_create(0, 4, 16, 1, 96, 0, C.byref(h)) == _lib.ERR_UNSUPPORTED
+    # group > 8 not built
+    q16 = torch.randn(2, 32, 128, device="cuda")
+    with pytest.raises(_lib.CloveError):
+        pool.decode(q16, bt, cl, max_ctx=64)
+
+
+def test_empty_batch_and_zero_max_ctx():
+    pool, bt, cl, q = _setup()
+    out = torch.full((2, 4, 128), 7.0, device="cuda")
+    cl0 = torch.zeros(2, dtype=torch.int32, device="cuda")
+    pool.decode(q, bt, cl0, max_ctx=0, out=out)
+    assert (out == 0).all()
+    e = torch.empty(0, 4, 128, device="cuda")
+    pool.decode(e, bt[:0], cl[:0], max_ctx=8)
+
+
+def test_pool_create_owns_memory():
+    import ctypes as C
+    L = _lib.lib()
+    h = C.c_void_p()
+    _lib.check(L.clove_cuda_pool_create(0, 128, 16, 8, 64, 160, C.byref(h)))
+    info = _lib.PoolInfo()
+    _lib.check(L.clove_cuda_pool_info(h, C.byref(info)))
+    assert info.owns_memory == 1 and info.plane_bytes == 128 * 16 * 8 * 64 * 2
+    assert info.v_cache - info.k_cache == info.plane_bytes
+    _lib.check(L.clove_cuda_pool_destroy(h))
