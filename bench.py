@@ -178,7 +178,11 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     spec = CONFIGS[args.config]
-    lay = make_layout(spec, seed=spec.seed + rank)  # weak scaling: one full workload per rank
+    # weak scaling: one full workload per rank (--batch shrinks it for profiling)
+    if args.batch is not None:
+        from dataclasses import replace
+        spec = replace(spec, num_blocks=0)  # pool sized to the blocks used
+    lay = make_layout(spec, seed=spec.seed + rank, batch=args.batch)
     pool = KVPool(lay.num_blocks, spec.block_size, spec.num_kv_heads, spec.head_dim, spec.dtype, dev)
     q, kn, vn, _ = fill_values(lay, dev, pool.storage)
     bt = torch.from_numpy(lay.block_tables).to(dev)
@@ -254,8 +258,10 @@ def run_ours(args) -> None:
     kv_bytes = lay.kv_bytes()  # per rank per step
     achieved = kv_bytes / (ms * 1e-3) / 1e9
     peak, peak_kind = _peaks()
-    _, case = host_sample_case(spec, args.cpu_seqs)
-    cb = cpu_arm(lay, case, args.cpu_seconds)
+    cb = None
+    if args.cpu_seconds > 0:
+        _, case = host_sample_case(spec, args.cpu_seqs)
+        cb = cpu_arm(lay, case, args.cpu_seconds)
     line = {
         "metric": METRIC, "value": tokens / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
@@ -281,11 +287,12 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2")
     ap.add_argument("--cpu-seqs", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=None, help="override the config batch (profiling only)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per decode launch from an ncu capture (reported as roofline.traffic)")

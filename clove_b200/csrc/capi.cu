@@ -112,6 +112,10 @@ static int check_pool_shape(int device, int num_blocks, int block_size, int num_
     set_last_error("pool shape (%d, %d, %d, %d) invalid", num_blocks, block_size, num_kv_heads, head_dim);
     return CLOVE_ERR_INVALID_ARG;
   }
+  if (block_size < 4 || (block_size & (block_size - 1))) {
+    set_last_error("block_size %d must be a power of two in [4, 256]", block_size);
+    return CLOVE_ERR_UNSUPPORTED;
+  }
   if (head_dim != 64 && head_dim != 128 && head_dim != 256) {
     set_last_error("head_dim %d not built (64, 128, 256)", head_dim);
     return CLOVE_ERR_UNSUPPORTED;

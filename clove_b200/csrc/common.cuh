@@ -155,6 +155,19 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named-barrier OR reduction: returns nonzero in every participating thread
+// if `pred` was nonzero in any of them.
+__device__ __forceinline__ int named_bar_or(int id, int nthreads, int pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\tselp.s32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -191,7 +204,8 @@ struct DecodeArgs {
   int max_ctx;
   int group;                 // query heads per KV head (runtime, <= template G)
   int append;                // 1: context_lens are pre-append lengths
-  int nstage;                // pipeline depth
+  int nstage;                // pipeline depth (a multiple of ncw)
+  int ncw;                   // consumer warps that take stages (<= the kernel's NCW)
   float qscale;              // scale * log2(e)
 };
 

@@ -34,16 +34,11 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "decode_common.cuh"
 #include "host.h"
 #include "mma_decode.cuh"
 
 namespace clove {
-
-__device__ __forceinline__ int clamp_ctx(const int32_t* ctx_lens, int b, int max_ctx, int append) {
-  int c = __ldg(ctx_lens + b);
-  c = max(0, min(c, max_ctx - append));
-  return c + append;
-}
 
 // ---------------------------------------------------------------------------
 // plan
@@ -104,192 +99,88 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
 }
 
 // ---------------------------------------------------------------------------
-// shared-memory carve-up of the decode kernels
-// ---------------------------------------------------------------------------
-struct SmemPlan {
-  int tile_stride;  // bytes of one [block_size, head_dim] tile, 128-aligned
-  int ring_bytes;   // nstage * 2 tiles
-  int bar_bytes;    // 2 * nstage mbarriers + misc ints
-  int scratch_bytes;
-  int total;        // + 128 alignment slack
-};
-
-__host__ __device__ inline SmemPlan smem_plan(int block_size, int head_dim, int elem_bytes, int nstage,
-                                             int scratch_bytes) {
-  SmemPlan s;
-  s.tile_stride = (block_size * head_dim * elem_bytes + 127) & ~127;
-  s.ring_bytes = 2 * s.tile_stride * nstage;
-  s.bar_bytes = ((2 * nstage * 8 + 64) + 127) & ~127;
-  s.scratch_bytes = (scratch_bytes + 127) & ~127;
-  s.total = s.ring_bytes + s.bar_bytes + s.scratch_bytes + 128;
-  return s;
-}
-
-// ---------------------------------------------------------------------------
 // the CUDA-core decode kernel
 // ---------------------------------------------------------------------------
 // T: KV/Q element type.  D: head_dim.  G: max query heads per KV head
-// (runtime a.group <= G).  NCW: consumer warps.  Each consumer warp owns
-// every NCW-th token of a tile, keeps a private (m, l, acc) state per query
-// head, and the warps are merged at the end of the unit.  Within a warp the
-// head_dim is split across lanes (E = D/32 elements each), so a score is a
-// lane-partial dot product plus a 5-step butterfly sum.
+// (runtime a.group <= G).  NCW: consumer warps.
+//
+// A stage (TT = 16 or block_size tokens) is consumed by one warp; warps take
+// a unit's stages round-robin and keep private (m, l, acc) softmax states,
+// merged in the epilogue.  Inside a warp, per pass of P = min(TT, 32) tokens:
+//   QK^T   lanes split the tokens: LPT = 32/P lanes per token, each lane
+//          covering D/LPT dims of its token's K row, with q (pre-scaled,
+//          f32) read from shared memory; an LPT-lane butterfly finishes the
+//          dot product.  Each lane walks its 16-byte chunks starting at a
+//          lane-dependent rotation so the 8 lanes of a shared-memory phase
+//          hit distinct banks.
+//   softmax the pass max is a warp max; the running max / correction are
+//          warp-uniform; the row sum l is kept per lane and reduced once per
+//          unit.
+//   P.V    lanes split head_dim (E = D/32 dims each); for every token the
+//          probability is broadcast with a shuffle and the V row is one
+//          conflict-free warp-wide shared-memory read.
 template <typename T, int D, int G, int NCW>
 __global__ void __launch_bounds__((NCW + 1) * 32)
     paged_decode_simt_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                              const DecodeArgs a) {
   constexpr int E = D / 32;
-  constexpr int TPW = 8;  // tokens per warp per sub-round
   constexpr int NCT = NCW * 32;
+  constexpr int EPC = 16 / (int)sizeof(T);  // elements per 16-byte chunk
   const int bs = a.block_size;
-  const int Hkv = a.num_kv_heads;
+  const int sb = bs >= 16 ? 1 : 16 / bs;
+  const int TT = sb * bs;
+  const int P = TT < 32 ? TT : 32;
+  const int LPT = 32 / P;
+  const int DL = D / LPT;
+  const int CH = DL / EPC;
   const int group = a.group;
-  const int Hq = Hkv * group;
-  const int tile_bytes = bs * D * (int)sizeof(T);
+  const int Hq = a.num_kv_heads * group;
 
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  const SmemPlan sp = smem_plan(bs, D, (int)sizeof(T), a.nstage, NCW * G * (D + 2) * 4);
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const SmemPlan sp =
+      smem_plan(bs, D, (int)sizeof(T), sb, a.nstage, (NCW * G * (D + 2) + G * D) * (int)sizeof(float));
   unsigned char* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.ring_bytes);
   uint64_t* empty = full + a.nstage;
-  volatile int* s_misc = reinterpret_cast<volatile int*>(empty + a.nstage);  // [0] abort, [1] last flag
+  volatile int* s_misc = reinterpret_cast<volatile int*>(empty + a.nstage);  // [0] abort, [1] last
   float* scratch = reinterpret_cast<float*>(smem + sp.ring_bytes + sp.bar_bytes);
+  float* qs = scratch + NCW * G * (D + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.nstage; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NCW);
+      mbar_init(&empty[s], 1);
     }
     s_misc[0] = 0;
     s_misc[1] = 0;
     fence_barrier_init();
   }
   __syncthreads();
-
-  const int n_units = *a.n_items * Hkv;
+  const int n_units = *a.n_items * a.num_kv_heads;
 
   if (warp == 0) {
-    // ------------------------------ producer ------------------------------
-    const uint64_t pol = policy_evict_first();
-    int stage = 0;
-    uint32_t phase = 0;
-    bool aborted = false;
-    for (int u = blockIdx.x; u < n_units && !aborted; u += gridDim.x) {
-      const int2 it = a.items[u / Hkv];
-      const int h = u - (u / Hkv) * Hkv;
-      const int b = it.x, c = it.y;
-      const int L = clamp_ctx(a.context_lens, b, a.max_ctx, a.append);
-      const int blk0 = c * a.chunk_blocks;
-      const int nblk = min(a.chunk_blocks, (L + bs - 1) / bs - blk0);
-      const int32_t* bt = a.block_tables + (size_t)b * a.bt_stride;
-      if (a.append && c == a.seq_chunks[b] - 1) {
-        // fused reshape-and-cache of the new token, head h
-        const int pos = L - 1;
-        int phys = __ldg(bt + pos / bs);
-        if (phys < 0 || phys >= a.num_blocks) {
-          if (lane == 0) atomicOr(a.err, CLOVE_FLAG_BLOCK_OOB);
-        } else {
-          const size_t row = (((size_t)phys * bs + (pos % bs)) * Hkv + h) * D;
-          const size_t src = ((size_t)b * Hkv + h) * D;
-          constexpr int WORDS = D * (int)sizeof(T) / 16;
-          const uint4* ks = reinterpret_cast<const uint4*>(static_cast<const T*>(a.k_new) + src);
-          const uint4* vs = reinterpret_cast<const uint4*>(static_cast<const T*>(a.v_new) + src);
-          uint4* kd = reinterpret_cast<uint4*>(static_cast<T*>(a.k_cache) + row);
-          uint4* vd = reinterpret_cast<uint4*>(static_cast<T*>(a.v_cache) + row);
-          for (int w = lane; w < WORDS; w += 32) {
-            kd[w] = __ldg(ks + w);
-            vd[w] = __ldg(vs + w);
-          }
-          fence_proxy_async_global();
-        }
-        __syncwarp();
-      }
-      for (int j0 = 0; j0 < nblk && !aborted; j0 += 32) {
-        int my = 0;
-        if (j0 + lane < nblk) {
-          my = __ldg(bt + blk0 + j0 + lane);
-          if (my < 0 || my >= a.num_blocks) {
-            atomicOr(a.err, CLOVE_FLAG_BLOCK_OOB);
-            my = 0;
-          }
-        }
-        const int cnt = min(32, nblk - j0);
-        for (int jj = 0; jj < cnt; ++jj) {
-          const int phys = __shfl_sync(0xffffffffu, my, jj);
-          int ok = 1;
-          if (lane == 0) {
-            if (s_misc[0] || !mbar_wait_bounded(&empty[stage], phase ^ 1, a.err)) {
-              ok = 0;
-              s_misc[0] = 1;
-            } else {
-              mbar_arrive_expect_tx(&full[stage], 2 * tile_bytes);
-              unsigned char* kt = ring + (size_t)stage * 2 * sp.tile_stride;
-              tma_load_3d(kt, &tm_k, &full[stage], 0, h, phys * bs, pol);
-              tma_load_3d(kt + sp.tile_stride, &tm_v, &full[stage], 0, h, phys * bs, pol);
-            }
-          }
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) {
-            aborted = true;
-            break;
-          }
-          if (++stage == a.nstage) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
-    }
-    if (aborted && lane == 0) {
-      // Drain: wait (bounded) for the copies of the last nstage issues to
-      // land before the CTA's shared memory goes away.  Walk back from the
-      // next (stage, phase) slot; issues before those have been waited on by
-      // the consumers already.
-      int s = stage;
-      uint32_t ph = phase;
-      for (int k = 0; k < a.nstage; ++k) {
-        if (--s < 0) {
-          s = a.nstage - 1;
-          ph ^= 1;
-        }
-        for (uint32_t i = 0; i < kWaitLimit; ++i)
-          if (mbar_try_wait(&full[s], ph)) break;
-      }
-    }
+    produce<T, D>(a, &tm_k, &tm_v, ring, sp, sb, full, empty, &s_misc[0], n_units);
     return;
   }
 
-  // ------------------------------ consumers -------------------------------
   const int cw = warp - 1;
   const int ct = threadIdx.x - 32;
-  int stage = 0;
-  uint32_t phase = 0;
+  const int tk_l = lane / LPT;    // token of this lane within a pass
+  const int part = lane % LPT;    // which D/LPT slice of that token
+  int gbase = 0;                  // stages of earlier units (CTA-wide count)
   float* my_scr = scratch + (size_t)cw * G * (D + 2);
 
   for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-    const int2 it = a.items[u / Hkv];
-    const int h = u - (u / Hkv) * Hkv;
-    const int b = it.x, c = it.y;
-    const int L = clamp_ctx(a.context_lens, b, a.max_ctx, a.append);
-    const int blk0 = c * a.chunk_blocks;
-    const int nblk = min(a.chunk_blocks, (L + bs - 1) / bs - blk0);
-    const int nchunks = a.seq_chunks[b];
-
-    float qr[G][E];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      if (g < group) {
-        const T* qp = static_cast<const T*>(a.q) + ((size_t)b * Hq + (size_t)h * group + g) * D + lane * E;
-        load_vec_f32<T, E>(qp, qr[g]);
-#pragma unroll
-        for (int e = 0; e < E; ++e) qr[g][e] *= a.qscale;
-      } else {
-#pragma unroll
-        for (int e = 0; e < E; ++e) qr[g][e] = 0.f;
-      }
+    const Unit x = load_unit(a, u, sb);
+    {
+      const T* qg = static_cast<const T*>(a.q) + ((size_t)x.b * Hq + (size_t)x.h * group) * D;
+      for (int i = ct; i < group * D; i += NCT) qs[i] = Elem<T>::to_f(qg[i]) * a.qscale;
     }
+    named_bar_sync(1, NCT);
+
     float m[G], l[G], acc[G][E];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -300,140 +191,108 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
     }
 
     bool aborted = false;
-    for (int j = 0; j < nblk; ++j) {
-      if (s_misc[0] || !mbar_wait_bounded(&full[stage], phase, a.err)) {
+    // Stage gs belongs to warp gs % ncw.  nstage is a multiple of ncw, so
+    // ring slot gs % nstage is only ever consumed by that warp, which takes
+    // its slots' fills in order: a parity wait can never alias an older,
+    // still-incomplete fill of the same slot.
+    const int ncw = a.ncw;
+    for (int j = cw < ncw ? ((cw - gbase) % ncw + ncw) % ncw : x.nstages; j < x.nstages; j += ncw) {
+      const int gs = gbase + j;
+      const int slot = gs % a.nstage;
+      const uint32_t par = (uint32_t)(gs / a.nstage) & 1u;
+      if (s_misc[0] || !mbar_wait_bounded(&full[slot], par, a.err)) {
         s_misc[0] = 1;
         aborted = true;
         break;
       }
-      const T* kt = reinterpret_cast<const T*>(ring + (size_t)stage * 2 * sp.tile_stride);
-      const T* vt = reinterpret_cast<const T*>(ring + (size_t)stage * 2 * sp.tile_stride + sp.tile_stride);
-      const int ntok = min(bs, L - (blk0 + j) * bs);
-      for (int t0 = 0; t0 < ntok; t0 += NCW * TPW) {
-        float sc[TPW][G];
-        float mloc[G];
+      const T* Ks = reinterpret_cast<const T*>(ring + (size_t)slot * sp.stage_bytes);
+      const T* Vs = reinterpret_cast<const T*>(ring + (size_t)slot * sp.stage_bytes + sb * sp.tile_stride);
+      const int ntok = min(TT, x.L - (x.blk0 + j * sb) * bs);
+      for (int p0 = 0; p0 < ntok; p0 += P) {
+        const int tk = p0 + tk_l;
+        // ---- scores ----
+        float s[G];
 #pragma unroll
-        for (int g = 0; g < G; ++g) mloc[g] = -INFINITY;
+        for (int g = 0; g < G; ++g) s[g] = 0.f;
+        const T* krow = Ks + (size_t)tk * D + part * DL;
+        const float* qrow = qs + part * DL;
+        for (int c = 0; c < CH; ++c) {
+          const int cc = (c + lane) & (CH - 1);
+          float kf[EPC];
+          load_vec_f32<T, EPC>(krow + cc * EPC, kf);
 #pragma unroll
-        for (int i = 0; i < TPW; ++i) {
-          const int t = t0 + cw + i * NCW;
-          if (t < ntok) {
-            float kv[E];
-            load_vec_f32<T, E>(kt + t * D + lane * E, kv);
+          for (int g = 0; g < G; ++g) {
+            if (g < group) {
+              const float4* q4 = reinterpret_cast<const float4*>(qrow + g * D + cc * EPC);
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-              float part = 0.f;
-#pragma unroll
-              for (int e = 0; e < E; ++e) part = fmaf(qr[g][e], kv[e], part);
-              sc[i][g] = warp_sum(part);
-              mloc[g] = fmaxf(mloc[g], sc[i][g]);
+              for (int v4 = 0; v4 < EPC / 4; ++v4) {
+                const float4 qq = q4[v4];
+                s[g] = fmaf(qq.x, kf[4 * v4 + 0], s[g]);
+                s[g] = fmaf(qq.y, kf[4 * v4 + 1], s[g]);
+                s[g] = fmaf(qq.z, kf[4 * v4 + 2], s[g]);
+                s[g] = fmaf(qq.w, kf[4 * v4 + 3], s[g]);
+              }
             }
-          } else {
-#pragma unroll
-            for (int g = 0; g < G; ++g) sc[i][g] = -INFINITY;
           }
         }
+        const bool valid = tk < ntok;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          const float mn = fmaxf(m[g], mloc[g]);
-          if (mn != -INFINITY) {
-            const float corr = exp2f(m[g] - mn);  // m = -inf -> 0
-            l[g] *= corr;
-#pragma unroll
-            for (int e = 0; e < E; ++e) acc[g][e] *= corr;
-            m[g] = mn;
-          }
+          for (int o = 1; o < LPT; o <<= 1) s[g] += __shfl_xor_sync(0xffffffffu, s[g], o);
+          s[g] = valid ? s[g] : -INFINITY;
         }
+        // ---- online softmax (warp-uniform max / correction) ----
+        float pe[G];
 #pragma unroll
-        for (int i = 0; i < TPW; ++i) {
-          const int t = t0 + cw + i * NCW;
-          if (t < ntok) {
-            float vv[E];
-            load_vec_f32<T, E>(vt + t * D + lane * E, vv);
+        for (int g = 0; g < G; ++g) {
+          float mp = s[g];
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-              const float p = exp2f(sc[i][g] - m[g]);
-              l[g] += p;
+          for (int o = 16; o > 0; o >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, o));
+          const float mn = fmaxf(m[g], mp);
+          const float corr = exp2f(m[g] - mn);
+          m[g] = mn;
+          l[g] *= corr;
 #pragma unroll
-              for (int e = 0; e < E; ++e) acc[g][e] = fmaf(p, vv[e], acc[g][e]);
-            }
+          for (int e = 0; e < E; ++e) acc[g][e] *= corr;
+          pe[g] = valid ? exp2f(s[g] - mn) : 0.f;
+          if (part == 0) l[g] += pe[g];
+        }
+        // ---- P.V ----
+        const int nt = min(P, ntok - p0);
+        const T* vbase = Vs + (size_t)p0 * D + lane * E;
+        for (int t = 0; t < nt; ++t) {
+          float vf[E];
+          load_vec_f32<T, E>(vbase + (size_t)t * D, vf);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float pt = __shfl_sync(0xffffffffu, pe[g], t * LPT);
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pt, vf[e], acc[g][e]);
           }
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-      if (++stage == a.nstage) {
-        stage = 0;
-        phase ^= 1;
-      }
+      if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    if (aborted) return;
+    // A consumer warp that met a stuck wait stops here; the reduction keeps
+    // every consumer thread on the same path (no one is left at a barrier).
+    if (named_bar_or(1, NCT, aborted ? 1 : 0)) return;
+    gbase += x.nstages;
 
-    // ---- merge the NCW warp states ----
+    // ---- publish this warp's state, merge, finish ----
 #pragma unroll
     for (int g = 0; g < G; ++g) {
+      const float lsum = warp_sum(l[g]);
 #pragma unroll
       for (int e = 0; e < E; ++e) my_scr[g * (D + 2) + lane * E + e] = acc[g][e];
       if (lane == 0) {
         my_scr[g * (D + 2) + D] = m[g];
-        my_scr[g * (D + 2) + D + 1] = l[g];
+        my_scr[g * (D + 2) + D + 1] = lsum;
       }
     }
     named_bar_sync(1, NCT);
-    float* part_base = a.partials + (((size_t)b * Hkv + h) * a.max_chunks) * G * (D + 2);
-    for (int idx = ct; idx < group * D; idx += NCT) {
-      const int g = idx / D, d = idx - (idx / D) * D;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < NCW; ++w) M = fmaxf(M, scratch[(w * G + g) * (D + 2) + D]);
-      float Ls = 0.f, O = 0.f;
-#pragma unroll
-      for (int w = 0; w < NCW; ++w) {
-        const float mw = scratch[(w * G + g) * (D + 2) + D];
-        if (mw != -INFINITY) {
-          const float f = exp2f(mw - M);
-          Ls = fmaf(scratch[(w * G + g) * (D + 2) + D + 1], f, Ls);
-          O = fmaf(scratch[(w * G + g) * (D + 2) + d], f, O);
-        }
-      }
-      if (nchunks == 1) {
-        a.out[((size_t)b * Hq + (size_t)h * group + g) * D + d] = O / Ls;
-      } else {
-        float* P = part_base + ((size_t)c * G + g) * (D + 2);
-        P[d] = O;
-        if (d == 0) {
-          P[D] = M;
-          P[D + 1] = Ls;
-        }
-      }
-    }
-    if (nchunks > 1) {
-      __threadfence();
-      named_bar_sync(1, NCT);
-      if (ct == 0) {
-        const int prev = atomicAdd(a.counters + (size_t)b * Hkv + h, 1);
-        s_misc[1] = (prev == nchunks - 1);
-      }
-      named_bar_sync(1, NCT);
-      if (s_misc[1]) {
-        __threadfence();
-        for (int idx = ct; idx < group * D; idx += NCT) {
-          const int g = idx / D, d = idx - (idx / D) * D;
-          float M = -INFINITY;
-          for (int cc = 0; cc < nchunks; ++cc) M = fmaxf(M, __ldcg(part_base + ((size_t)cc * G + g) * (D + 2) + D));
-          float Ls = 0.f, O = 0.f;
-          for (int cc = 0; cc < nchunks; ++cc) {
-            const float* P = part_base + ((size_t)cc * G + g) * (D + 2);
-            const float f = exp2f(__ldcg(P + D) - M);
-            Ls = fmaf(__ldcg(P + D + 1), f, Ls);
-            O = fmaf(__ldcg(P + d), f, O);
-          }
-          a.out[((size_t)b * Hq + (size_t)h * group + g) * D + d] = O / Ls;
-        }
-        if (ct == 0) a.counters[(size_t)b * Hkv + h] = 0;
-      }
-    }
-    named_bar_sync(1, NCT);  // scratch and s_misc[1] are reused by the next unit
+    finish_unit<D, G, NCW, NCT>(a, x, scratch, &s_misc[1], ct);
+    named_bar_sync(1, NCT);  // scratch, q and s_misc[1] are reused by the next unit
   }
 }
 
@@ -488,18 +347,28 @@ DecodeLayout decode_layout(const clove_pool& pool, int batch, int num_q_heads, i
 template <typename T, int D, int G>
 static int run_simt(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
   auto kern = paged_decode_simt_kernel<T, D, G, kNCW>;
-  const int scratch = kNCW * G * (D + 2) * 4;
-  const int tile = (pool.block_size * D * (int)sizeof(T) + 127) & ~127;
-  int nstage = kRingTarget / (2 * tile);
-  if (nstage < 2) nstage = 2;
-  if (nstage > 16) nstage = 16;
-  SmemPlan sp = smem_plan(pool.block_size, D, sizeof(T), nstage, scratch);
-  while (sp.total > 200 * 1024 && nstage > 2) {
-    --nstage;
-    sp = smem_plan(pool.block_size, D, sizeof(T), nstage, scratch);
+  const int bs = pool.block_size;
+  const int sb = bs >= 16 ? 1 : 16 / bs;
+  const int scratch = (kNCW * G * (D + 2) + G * D) * 4;
+  SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch);
+  // nstage: a multiple of the number of consumer warps that take stages (see
+  // the kernel); large tiles use fewer of them.
+  int ncw = kNCW;
+  int nstage = (kRingTarget / sp.stage_bytes) / ncw * ncw;
+  if (nstage < ncw) nstage = ncw;
+  if (nstage > 4 * ncw) nstage = 4 * ncw;
+  sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch);
+  while (sp.total > 200 * 1024 && nstage > 1) {
+    if (nstage > ncw) {
+      nstage -= ncw;
+    } else {
+      ncw = --nstage;
+    }
+    sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch);
   }
+  a.ncw = ncw;
   if (sp.total > 227 * 1024) {
-    set_last_error("paged_decode: block_size %d x head_dim %d tile does not fit shared memory", pool.block_size, D);
+    set_last_error("paged_decode: block_size %d x head_dim %d tile does not fit shared memory", bs, D);
     return CLOVE_ERR_UNSUPPORTED;
   }
   a.nstage = nstage;
@@ -615,6 +484,7 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   a.group = call.num_q_heads / pool.num_kv_heads;
   a.append = append;
   a.nstage = 2;
+  a.ncw = 1;
   a.qscale = call.scale * kLog2e;
 
   switch (pool.dtype) {
