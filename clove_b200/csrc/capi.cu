@@ -47,7 +47,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-static int encode_plane_map(CUtensorMap* map, void* base, const clove_pool& p) {
+static int encode_plane_map(CUtensorMap* map, void* base, const clove_pool& p, bool swizzled) {
   auto fn = encode_fn();
   if (!fn) {
     set_last_error("cuTensorMapEncodeTiled unavailable from the driver");
@@ -61,10 +61,11 @@ static int encode_plane_map(CUtensorMap* map, void* base, const clove_pool& p) {
                         (cuuint64_t)p.num_blocks * (cuuint64_t)p.block_size};
   cuuint64_t strides[2] = {(cuuint64_t)p.head_dim * p.elem_bytes,
                            (cuuint64_t)p.num_kv_heads * p.head_dim * p.elem_bytes};
-  cuuint32_t box[3] = {(cuuint32_t)p.head_dim, 1u, (cuuint32_t)p.block_size};
+  cuuint32_t box[3] = {(cuuint32_t)(swizzled ? 64 : p.head_dim), 1u, (cuuint32_t)p.block_size};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, dt, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  swizzled ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_last_error("cuTensorMapEncodeTiled failed (%d) for head_dim %d block_size %d", (int)r, p.head_dim,
@@ -140,9 +141,19 @@ static int finish_pool(clove_pool* p) {
   if (e != cudaSuccess) return cuda_fail("cudaMalloc(flags)", e);
   e = cudaMemset(p->flags, 0, 256);
   if (e != cudaSuccess) return cuda_fail("cudaMemset(flags)", e);
-  int rc = encode_plane_map(&p->tm_k, p->k_cache, *p);
+  int rc = encode_plane_map(&p->tm_k, p->k_cache, *p, false);
   if (rc) return rc;
-  return encode_plane_map(&p->tm_v, p->v_cache, *p);
+  rc = encode_plane_map(&p->tm_v, p->v_cache, *p, false);
+  if (rc) return rc;
+  p->has_swizzled = 0;
+  if (p->elem_bytes == 2 && p->head_dim % 64 == 0 && p->block_size >= 8) {
+    rc = encode_plane_map(&p->tm_k_sw, p->k_cache, *p, true);
+    if (rc) return rc;
+    rc = encode_plane_map(&p->tm_v_sw, p->v_cache, *p, true);
+    if (rc) return rc;
+    p->has_swizzled = 1;
+  }
+  return CLOVE_OK;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -101,7 +101,11 @@ __device__ __forceinline__ void append_row(const DecodeArgs& a, const Unit& x, i
 // the ring.  Only lane 0 issues copies; the warp loads block-table entries 32
 // at a time and broadcasts them.  On a stuck wait it raises the abort flag and
 // drains its own in-flight copies (bounded) before returning.
-template <typename T, int D>
+//
+// NBOX: boxes per tile.  1 = one [block_size, head_dim] box (dense rows);
+// D/64 = head_dim split into 64-element (128-byte) boxes written with the
+// 128-byte swizzle, sub-tile hb at tile offset hb * block_size * 128.
+template <typename T, int D, int NBOX>
 __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                         unsigned char* ring, const SmemPlan& sp, int sb, uint64_t* full, uint64_t* empty,
                         volatile int* s_abort, int n_units) {
@@ -144,8 +148,14 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             if (i < nb) {
-              tma_load_3d(st + i * sp.tile_stride, tm_k, &full[slot], 0, x.h, phys[i] * bs, pol);
-              tma_load_3d(st + (sb + i) * sp.tile_stride, tm_v, &full[slot], 0, x.h, phys[i] * bs, pol);
+#pragma unroll
+              for (int hb = 0; hb < NBOX; ++hb) {
+                const int off = hb * (D / NBOX) * (int)sizeof(T) * bs;
+                tma_load_3d(st + i * sp.tile_stride + off, tm_k, &full[slot], hb * (D / NBOX), x.h, phys[i] * bs,
+                            pol);
+                tma_load_3d(st + (sb + i) * sp.tile_stride + off, tm_v, &full[slot], hb * (D / NBOX), x.h,
+                            phys[i] * bs, pol);
+              }
             }
           }
         }

@@ -162,7 +162,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   const int n_units = *a.n_items * a.num_kv_heads;
 
   if (warp == 0) {
-    produce<T, D>(a, &tm_k, &tm_v, ring, sp, sb, full, empty, &s_misc[0], n_units);
+    produce<T, D, 1>(a, &tm_k, &tm_v, ring, sp, sb, full, empty, &s_misc[0], n_units);
     return;
   }
 
@@ -399,12 +399,13 @@ static int dispatch_group(const clove_pool& pool, DecodeArgs& a, cudaStream_t st
   const int g = a.group;
   const int variant = decode_variant();
   if constexpr (!std::is_same<T, float>::value) {
-    if ((variant == 2 || (variant == 0 && g >= 4)) && g <= 8 && mma_supported<D>()) {
-      return run_mma<T, D>(pool, a, stream);
+    if constexpr (mma_supported<D>()) {
+      const bool ok = g <= 8 && pool.has_swizzled && pool.block_size >= 8;
+      if (ok && (variant == 2 || (variant == 0 && g >= 4))) return run_mma<T, D>(pool, a, stream);
     }
   }
   if (variant == 2) {
-    set_last_error("paged_decode: tensor-core variant needs bf16/f16 and 4 <= group <= 8 (group %d)", g);
+    set_last_error("paged_decode: tensor-core variant needs bf16/f16, head_dim 64/128, block_size >= 8, group <= 8 (group %d)", g);
     return CLOVE_ERR_UNSUPPORTED;
   }
   if (g == 1) return run_simt<T, D, 1>(pool, a, stream);

@@ -25,6 +25,11 @@ struct clove_pool {
   int num_sms;
   CUtensorMap tm_k;  // 3-D maps {head_dim, num_kv_heads, num_blocks*block_size}
   CUtensorMap tm_v;
+  // 16-bit pools only: head_dim split into 64-element boxes with the 128-byte
+  // swizzle (the tensor-core kernel's conflict-free shared-memory layout).
+  CUtensorMap tm_k_sw;
+  CUtensorMap tm_v_sw;
+  int has_swizzled;
 };
 
 namespace clove {

@@ -1,1 +1,322 @@
+// Tensor-core decode consumer for 16-bit KV (bf16 / f16) and GQA groups of
+// 4..8 query heads per KV head, head_dim 64 or 128.
+//
+// Why tensor cores here: with a group of G query heads every K/V element
+// feeds G multiply-adds in QK^T and again in P.V, 2G flop per byte for
+// 16-bit data; at HBM speed (~6.5 TB/s) a group of 8 needs ~100 TFLOP/s,
+// beyond what the CUDA cores sustain next to the softmax.  The query rows of
+// one KV head form a real (if short) dense tile, so a warp-level
+// m16n8k16 MMA handles them: M = 16 query rows (G real, the rest zero),
+// N = 8 tokens (QK^T) or 8 dims (P.V), K = 16 dims (QK^T) or 16 tokens (P.V).
+// The score fragment of QK^T is, register for register, the A operand of
+// P.V, so probabilities never leave registers.
+//
+// Shared memory: each [block_size, head_dim] tile arrives as head_dim/64
+// sub-tiles of [block_size, 64] elements (128-byte rows) written by the bulk
+// tensor copy with the 128-byte swizzle: 16-byte chunk c of row r sits at
+// chunk c ^ (r & 7).  ldmatrix reads (8 rows x 16 bytes per matrix) are then
+// conflict-free.
+//
+// Pipeline, work units, ring-slot ownership and the epilogue are those of
+// the CUDA-core kernel (decode_common.cuh).
+#include "common.cuh"
+#include "decode_common.cuh"
+#include "host.h"
 #include "mma_decode.cuh"
+
+namespace clove {
+
+template <typename T> struct MmaType;
+template <> struct MmaType<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+template <> struct MmaType<__half> {
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+};
+
+// D(16x8, f32) += A(16x16) * B(16x8); A rows 8..15 are zero (registers a1,
+// a3 = 0), so only d0, d1 (row lane/4) carry results; d2, d3 stay zero.
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  const uint32_t z = 0;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Byte offset, inside a stage's K (or V) region, of 16-byte chunk `ch`
+// (head_dim / 8 chunks per token) of token `tok` (0 .. sb*block_size-1).
+__device__ __forceinline__ uint32_t swz_off(int tok, int ch, int bs, int tile_stride) {
+  const int blk = tok / bs, r = tok - blk * bs;
+  const int hb = ch >> 3, c = ch & 7;
+  return (uint32_t)(blk * tile_stride + (hb * bs + r) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// NCW consumer warps; D = 64 or 128.  Each consumer warp owns whole stages;
+// per pass of 16 tokens: S = Q K^T (2 n-tiles x D/16 k-steps), online
+// softmax on the score fragment, O += P V (D/8 n-tiles).
+template <typename T, int D, int NCW>
+__global__ void __launch_bounds__((NCW + 1) * 32)
+    paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                            const DecodeArgs a) {
+  constexpr int G = 8;              // rows of the per-KV-head query tile that can be real
+  constexpr int KS = D / 16;        // k-steps of QK^T
+  constexpr int NT = D / 8;         // n-tiles of P.V
+  constexpr int NCT = NCW * 32;
+  const int bs = a.block_size;
+  const int sb = bs >= 16 ? 1 : 16 / bs;
+  const int TT = sb * bs;
+  const int group = a.group;
+  const int Hq = a.num_kv_heads * group;
+
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const SmemPlan sp = smem_plan(bs, D, (int)sizeof(T), sb, a.nstage, NCW * G * (D + 2) * (int)sizeof(float));
+  unsigned char* ring = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.ring_bytes);
+  uint64_t* empty = full + a.nstage;
+  volatile int* s_misc = reinterpret_cast<volatile int*>(empty + a.nstage);
+  float* scratch = reinterpret_cast<float*>(smem + sp.ring_bytes + sp.bar_bytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.nstage; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    s_misc[0] = 0;
+    s_misc[1] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int n_units = *a.n_items * a.num_kv_heads;
+
+  if (warp == 0) {
+    produce<T, D, D / 64>(a, &tm_k, &tm_v, ring, sp, sb, full, empty, &s_misc[0], n_units);
+    return;
+  }
+
+  const int cw = warp - 1;
+  const int ct = threadIdx.x - 32;
+  const int g = lane >> 2;      // query row of this lane's fragment values
+  const int tq = lane & 3;      // column pair within an 8-wide n-tile
+  const int mi = lane >> 3;     // ldmatrix: which 8x8 matrix this lane addresses
+  const int mr = lane & 7;      // ldmatrix: which row of it
+  const float sl2 = a.qscale;   // scale * log2(e), applied to the f32 scores
+  int gbase = 0;
+  float* my_scr = scratch + (size_t)cw * G * (D + 2);
+
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const Unit x = load_unit(a, u, sb);
+    // Q fragments (A operand rows = query heads of this KV head), unscaled.
+    uint32_t qa[KS][2];
+    {
+      const T* qrow = static_cast<const T*>(a.q) + ((size_t)x.b * Hq + (size_t)x.h * group + g) * D;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+        if (g < group) {
+          qa[k][0] = *reinterpret_cast<const uint32_t*>(qrow + k * 16 + 2 * tq);
+          qa[k][1] = *reinterpret_cast<const uint32_t*>(qrow + k * 16 + 8 + 2 * tq);
+        } else {
+          qa[k][0] = 0u;
+          qa[k][1] = 0u;
+        }
+      }
+    }
+    float m = -INFINITY, l = 0.f;
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+    bool aborted = false;
+    const int ncw = a.ncw;
+    // Stage ownership as in the CUDA-core kernel: stage gs -> warp gs % ncw.
+    for (int j = cw < ncw ? ((cw - gbase) % ncw + ncw) % ncw : x.nstages; j < x.nstages; j += ncw) {
+      const int gs = gbase + j;
+      const int slot = gs % a.nstage;
+      const uint32_t par = (uint32_t)(gs / a.nstage) & 1u;
+      if (s_misc[0] || !mbar_wait_bounded(&full[slot], par, a.err)) {
+        s_misc[0] = 1;
+        aborted = true;
+        break;
+      }
+      unsigned char* kst = ring + (size_t)slot * sp.stage_bytes;
+      unsigned char* vst = kst + sb * sp.tile_stride;
+      const int ntok = min(TT, x.L - (x.blk0 + j * sb) * bs);
+      if (ntok < TT) {
+        // Rows past the context may hold any bits (even NaN patterns); P is
+        // zero there but 0 * NaN is NaN inside the MMA, so clear those V rows.
+        for (int i = lane; i < (TT - ntok) * (D / 8); i += 32) {
+          const int tok = ntok + i / (D / 8), ch = i % (D / 8);
+          *reinterpret_cast<uint4*>(vst + swz_off(tok, ch, bs, sp.tile_stride)) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      const uint32_t kbase = smem_u32(kst), vbase = smem_u32(vst);
+      for (int p0 = 0; p0 < ntok; p0 += 16) {
+        // ---- S = Q K^T for tokens p0 .. p0+15 ----
+        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+          // matrices: (tok 0-7, d 0-7), (tok 0-7, d 8-15), (tok 8-15, d 0-7), (tok 8-15, d 8-15)
+          uint32_t b[4];
+          ldsm_x4(kbase + swz_off(p0 + (mi >> 1) * 8 + mr, 2 * k + (mi & 1), bs, sp.tile_stride), b);
+          mma16816<T>(sacc[0], qa[k][0], qa[k][1], b[0], b[1]);
+          mma16816<T>(sacc[1], qa[k][0], qa[k][1], b[2], b[3]);
+        }
+        // ---- online softmax on rows g (values c0, c1 of each n-tile) ----
+        float s[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = p0 + (e >> 1) * 8 + 2 * tq + (e & 1);
+          s[e] = tok < ntok ? sacc[e >> 1][e & 1] * sl2 : -INFINITY;
+        }
+        float mx = fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m, mx);
+        const float corr = exp2f(m - mn);
+        m = mn;
+        float pr[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pr[e] = exp2f(s[e] - mn);
+        l = l * corr + (pr[0] + pr[1]) + (pr[2] + pr[3]);
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          o[n][0] *= corr;
+          o[n][1] *= corr;
+        }
+        const uint32_t pa0 = MmaType<T>::pack(pr[0], pr[1]);  // P[g][2tq, 2tq+1]
+        const uint32_t pa2 = MmaType<T>::pack(pr[2], pr[3]);  // P[g][8+2tq, 8+2tq+1]
+        // ---- O += P V for tokens p0 .. p0+15 ----
+#pragma unroll
+        for (int n = 0; n < NT; n += 2) {
+          // matrices: (tok 0-7, d n*8..), (tok 8-15, d n*8..), (tok 0-7, d n*8+8..), (tok 8-15, d n*8+8..)
+          uint32_t b[4];
+          ldsm_x4_trans(vbase + swz_off(p0 + (mi & 1) * 8 + mr, n + (mi >> 1), bs, sp.tile_stride), b);
+          mma16816<T>(o[n], pa0, pa2, b[0], b[1]);
+          mma16816<T>(o[n + 1], pa0, pa2, b[2], b[3]);
+        }
+      }
+      if (ntok < TT) fence_proxy_async_smem();  // order the zero-fill before the slot's next bulk copy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (named_bar_or(1, NCT, aborted ? 1 : 0)) return;
+    gbase += x.nstages;
+
+    // ---- publish (acc, m, l) of rows g < group; rows of idle warps stay -inf ----
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (g < group) {
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        my_scr[g * (D + 2) + n * 8 + 2 * tq] = o[n][0];
+        my_scr[g * (D + 2) + n * 8 + 2 * tq + 1] = o[n][1];
+      }
+      if (tq == 0) {
+        my_scr[g * (D + 2) + D] = m;
+        my_scr[g * (D + 2) + D + 1] = l;
+      }
+    }
+    named_bar_sync(1, NCT);
+    finish_unit<D, G, NCW, NCT>(a, x, scratch, &s_misc[1], ct);
+    named_bar_sync(1, NCT);
+  }
+}
+
+constexpr int kMmaNCW = 4;
+constexpr int kMmaRingTarget = 96 * 1024;
+
+template <typename T, int D>
+int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
+  if (!pool.has_swizzled || pool.block_size < 8 || a.group > 8) {
+    set_last_error("paged_decode: tensor-core kernel needs a 16-bit pool, block_size >= 8, group <= 8");
+    return CLOVE_ERR_UNSUPPORTED;
+  }
+  auto kern = paged_decode_mma_kernel<T, D, kMmaNCW>;
+  const int bs = pool.block_size;
+  const int sb = bs >= 16 ? 1 : 16 / bs;
+  const int scratch = kMmaNCW * 8 * (D + 2) * 4;
+  SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch);
+  int ncw = kMmaNCW;
+  int nstage = (kMmaRingTarget / sp.stage_bytes) / ncw * ncw;
+  if (nstage < ncw) nstage = ncw;
+  if (nstage > 4 * ncw) nstage = 4 * ncw;
+  sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch);
+  while (sp.total + 1024 > 200 * 1024 && nstage > 1) {
+    if (nstage > ncw) {
+      nstage -= ncw;
+    } else {
+      ncw = --nstage;
+    }
+    sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch);
+  }
+  const int smem = sp.total + 1024;  // 1024-byte alignment slack for the swizzled ring
+  if (smem > 227 * 1024) {
+    set_last_error("paged_decode: block_size %d x head_dim %d tile does not fit shared memory", bs, D);
+    return CLOVE_ERR_UNSUPPORTED;
+  }
+  a.nstage = nstage;
+  a.ncw = ncw;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_last_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    return CLOVE_ERR_CUDA;
+  }
+  int occ = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, (kMmaNCW + 1) * 32, smem);
+  if (e != cudaSuccess || occ < 1) occ = 1;
+  long long units_max = (long long)a.batch * a.max_chunks * a.num_kv_heads;
+  long long grid = (long long)pool.num_sms * occ;
+  if (grid > units_max) grid = units_max;
+  if (grid < 1) grid = 1;
+  kern<<<(unsigned)grid, (kMmaNCW + 1) * 32, smem, stream>>>(pool.tm_k_sw, pool.tm_v_sw, a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error("paged_decode (mma) launch: %s", cudaGetErrorString(e));
+    return CLOVE_ERR_CUDA;
+  }
+  count_launches(1);
+  return CLOVE_OK;
+}
+
+template int run_mma<__nv_bfloat16, 64>(const clove_pool&, DecodeArgs&, cudaStream_t);
+template int run_mma<__nv_bfloat16, 128>(const clove_pool&, DecodeArgs&, cudaStream_t);
+template int run_mma<__half, 64>(const clove_pool&, DecodeArgs&, cudaStream_t);
+template int run_mma<__half, 128>(const clove_pool&, DecodeArgs&, cudaStream_t);
+
+}  // namespace clove

@@ -8,7 +8,7 @@ namespace clove {
 
 template <int D>
 constexpr bool mma_supported() {
-  return false;
+  return D == 64 || D == 128;
 }
 
 template <typename T, int D>

@@ -83,3 +83,38 @@ def test_long_context_split_chunks():
     from clove_b200.workload import Spec, make_layout
     spec = Spec("t", 2, 16, 2, 128, 32, 0, torch.bfloat16, "uniform", 60000, 70000, "permutation", seed=14)
     run_layout_vs_oracle(make_layout(spec), 2e-2)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("group", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("bs", [8, 16, 32])
+def test_tensor_core_variant_forced(d, dtype, group, bs):
+    from clove_b200 import set_decode_variant
+    from clove_b200.workload import Spec, make_layout
+    spec = Spec("t", 3, 2 * group, 2, d, bs, 0, dtype, "uniform", 1, 500, "permutation", seed=15)
+    set_decode_variant("mma")
+    try:
+        run_layout_vs_oracle(make_layout(spec), RT[dtype])
+    finally:
+        set_decode_variant("auto")
+
+
+def test_tensor_core_nan_rows_past_context():
+    # Pool memory past the context holds NaN bit patterns; the output must
+    # not see them (P is zero there and the tensor-core kernel clears V rows).
+    from clove_b200 import KVPool
+    from clove_b200.workload import Spec, fill_values, make_layout
+    spec = Spec("t", 4, 16, 2, 128, 32, 0, torch.bfloat16, "uniform", 1, 90, "permutation", seed=16)
+    lay = make_layout(spec)
+    dev = torch.device("cuda", 0)
+    pool = KVPool(lay.num_blocks, 32, 2, 128, torch.bfloat16, 0)
+    q, kn, vn, _ = fill_values(lay, dev, pool.storage)
+    # poison every slot past each sequence's (post-append) length
+    for b in range(lay.batch):
+        L = int(lay.context_lens[b]) + 1
+        blk = int(lay.block_tables[b, (L - 1) // 32])
+        pool.storage[:, blk, (L - 1) % 32 + 1:] = float("nan")
+    out = pool.append_decode(q, kn, vn, torch.from_numpy(lay.block_tables).to(dev),
+                             torch.from_numpy(lay.context_lens).to(dev), max_ctx=lay.max_ctx)
+    assert torch.isfinite(out).all()

@@ -41,8 +41,8 @@ def _i32(a):
     return torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(_dev())
 
 
-@pytest.mark.parametrize("name", GOLDEN)
-@pytest.mark.parametrize("variant", ["auto", "simt"])
+@pytest.mark.parametrize("name,variant", [(n, v) for n in GOLDEN for v in ("auto", "simt")] +
+                         [("bf16_gqa_bs32", "mma")])
 def test_golden_append_decode(name, variant):
     from clove_b200 import set_decode_variant
     from workload_check import bits_equal, tol_check
