@@ -199,7 +199,7 @@ struct DecodeArgs {
   int num_kv_heads;
   int num_blocks;
   int block_size;
-  int chunk_blocks;          // blocks per work item
+  const int32_t* chunk_blocks;  // device scalar: blocks per work item (set by the plan)
   int max_chunks;            // chunks per sequence, upper bound
   int max_ctx;
   int group;                 // query heads per KV head (runtime, <= template G)
@@ -220,7 +220,10 @@ struct PlanArgs {
   int batch;
   int num_kv_heads;
   int row_floats;  // Hq * D: output floats per sequence
-  int chunk_tokens;
+  int block_size;
+  int min_chunk_blocks;      // lower bound on blocks per work item
+  long long target_units;    // work units the chunk size aims for
+  int32_t* chunk_blocks;     // out: blocks per work item chosen for this call
   int max_ctx;
   int append;
 };

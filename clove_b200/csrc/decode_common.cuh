@@ -35,8 +35,9 @@ __device__ __forceinline__ Unit load_unit(const DecodeArgs& a, int u, int sb) {
   x.b = it.x;
   x.c = it.y;
   x.L = clamp_ctx(a.context_lens, x.b, a.max_ctx, a.append);
-  x.blk0 = x.c * a.chunk_blocks;
-  x.nblk = min(a.chunk_blocks, (x.L + a.block_size - 1) / a.block_size - x.blk0);
+  const int cb = __ldg(a.chunk_blocks);
+  x.blk0 = x.c * cb;
+  x.nblk = min(cb, (x.L + a.block_size - 1) / a.block_size - x.blk0);
   x.nstages = (x.nblk + sb - 1) / sb;
   return x;
 }

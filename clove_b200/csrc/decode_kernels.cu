@@ -49,11 +49,29 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
   __shared__ int warp_tot[32];
   __shared__ int s_base;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ long long s_blocks;
   if (tid == 0) {
     s_base = 0;
+    s_blocks = 0;
     *p.err = 0;  // flags report the most recent call only
   }
   __syncthreads();
+  // Chunk size from the actual work: total (block, KV head) pairs spread
+  // over ~target_units work items, never below min_chunk_blocks.
+  {
+    long long mine = 0;
+    for (int b = tid; b < p.batch; b += kPlanThreads) {
+      const int L = clamp_ctx(p.context_lens, b, p.max_ctx, p.append);
+      mine += (L + p.block_size - 1) / p.block_size;
+    }
+    for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+    if (lane == 0 && mine) atomicAdd(reinterpret_cast<unsigned long long*>(&s_blocks), (unsigned long long)mine);
+  }
+  __syncthreads();
+  const long long want = (s_blocks * p.num_kv_heads + p.target_units - 1) / p.target_units;
+  const int cb = (int)max((long long)p.min_chunk_blocks, want);
+  const int chunk_tokens = cb * p.block_size;
+  if (tid == 0) *p.chunk_blocks = cb;
   for (int base = 0; base < p.batch; base += kPlanThreads) {
     const int b = base + tid;
     int n = 0;
@@ -61,7 +79,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
       int raw = p.context_lens[b];
       int L = clamp_ctx(p.context_lens, b, p.max_ctx, p.append);
       if (raw != L - p.append) atomicOr(p.err, CLOVE_FLAG_CTX_RANGE);
-      n = (L + p.chunk_tokens - 1) / p.chunk_tokens;
+      n = (L + chunk_tokens - 1) / chunk_tokens;
       p.seq_chunks[b] = n;
       for (int h = 0; h < p.num_kv_heads; ++h) p.counters[(size_t)b * p.num_kv_heads + h] = 0;
       if (L == 0) {
@@ -302,19 +320,10 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
 constexpr int kNCW = 4;          // consumer warps of the CUDA-core kernel
 constexpr int kRingTarget = 96 * 1024;
 
-static int chunk_blocks_for(int batch, int hkv, int max_ctx, int block_size, int sms) {
-  const int max_blocks = (max_ctx + block_size - 1) / block_size;
-  if (max_blocks <= 0) return 1;
-  const long long units1 = (long long)batch * hkv;
-  const long long target = (long long)sms * 8;  // ~4 waves of 2 resident CTAs per SM
-  if (units1 >= target) return max_blocks;
-  long long nchunks = (target + units1 - 1) / units1;
-  int cb = (int)((max_blocks + nchunks - 1) / nchunks);
-  const int min_blocks = (256 + block_size - 1) / block_size;  // >= 256 tokens per chunk
-  if (cb < min_blocks) cb = min_blocks;
-  if (cb > max_blocks) cb = max_blocks;
-  return cb;
-}
+// Smallest work item: 256 tokens (a chunk shorter than that spends more on
+// its epilogue than on streaming).  The plan kernel picks the actual chunk
+// size per call from the total work; this bound sizes the workspace.
+static int min_chunk_blocks(int block_size) { return (256 + block_size - 1) / block_size; }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -322,7 +331,7 @@ DecodeLayout decode_layout(const clove_pool& pool, int batch, int num_q_heads, i
   DecodeLayout L;
   const int hkv = pool.num_kv_heads;
   const int group = num_q_heads / hkv;
-  L.chunk_blocks = chunk_blocks_for(batch, hkv, max_ctx, pool.block_size, pool.num_sms);
+  L.chunk_blocks = min_chunk_blocks(pool.block_size);
   const int max_blocks = (max_ctx + pool.block_size - 1) / pool.block_size;
   L.max_chunks = max_blocks <= 0 ? 1 : (max_blocks + L.chunk_blocks - 1) / L.chunk_blocks;
   size_t off = 0;
@@ -448,7 +457,10 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   p.batch = call.batch;
   p.num_kv_heads = pool.num_kv_heads;
   p.row_floats = call.num_q_heads * pool.head_dim;
-  p.chunk_tokens = L.chunk_blocks * pool.block_size;
+  p.block_size = pool.block_size;
+  p.min_chunk_blocks = L.chunk_blocks;
+  p.target_units = (long long)pool.num_sms * 8;  // ~4 units per resident CTA at 2 CTAs/SM
+  p.chunk_blocks = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 1;
   p.max_ctx = call.max_ctx;
   p.append = append;
   plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
@@ -479,7 +491,7 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   a.num_kv_heads = pool.num_kv_heads;
   a.num_blocks = pool.num_blocks;
   a.block_size = pool.block_size;
-  a.chunk_blocks = L.chunk_blocks;
+  a.chunk_blocks = p.chunk_blocks;
   a.max_chunks = L.max_chunks;
   a.max_ctx = call.max_ctx;
   a.group = call.num_q_heads / pool.num_kv_heads;

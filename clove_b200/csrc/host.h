@@ -36,8 +36,8 @@ namespace clove {
 
 // Workspace carve-up for one decode call; offsets in bytes from the base.
 struct DecodeLayout {
-  int chunk_blocks;
-  int max_chunks;
+  int chunk_blocks;  // the smallest chunk the plan may choose
+  int max_chunks;    // chunks per sequence at that size (workspace bound)
   size_t off_err, off_nitems, off_items, off_seq_chunks, off_counters, off_partials;
   size_t total;
 };

@@ -186,14 +186,23 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         __syncwarp();
       }
       const uint32_t kbase = smem_u32(kst), vbase = smem_u32(vst);
+      const int hb_bytes = bs * 128;  // one 64-dim sub-tile
       for (int p0 = 0; p0 < ntok; p0 += 16) {
+        // Per-pass ldmatrix row addresses: chunk ch of token tok lives at
+        // row_off(tok) + (ch >> 3) * hb_bytes + (((ch & 7) ^ (tok_row & 7)) << 4).
+        const int tk_k = p0 + (mi >> 1) * 8 + mr, tk_v = p0 + (mi & 1) * 8 + mr;
+        const int bk = tk_k / bs, rk = tk_k - bk * bs;
+        const int bv = tk_v / bs, rv = tk_v - bv * bs;
+        const uint32_t krow = kbase + (uint32_t)(bk * sp.tile_stride + rk * 128), kx = (uint32_t)(rk & 7);
+        const uint32_t vrow = vbase + (uint32_t)(bv * sp.tile_stride + rv * 128), vx = (uint32_t)(rv & 7);
+        const uint32_t kc = (uint32_t)(mi & 1), vc = (uint32_t)(mi >> 1);
         // ---- S = Q K^T for tokens p0 .. p0+15 ----
         float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
         for (int k = 0; k < KS; ++k) {
           // matrices: (tok 0-7, d 0-7), (tok 0-7, d 8-15), (tok 8-15, d 0-7), (tok 8-15, d 8-15)
           uint32_t b[4];
-          ldsm_x4(kbase + swz_off(p0 + (mi >> 1) * 8 + mr, 2 * k + (mi & 1), bs, sp.tile_stride), b);
+          ldsm_x4(krow + (uint32_t)((k >> 2) * hb_bytes) + (((((uint32_t)(2 * k) & 7u) + kc) ^ kx) << 4), b);
           mma16816<T>(sacc[0], qa[k][0], qa[k][1], b[0], b[1]);
           mma16816<T>(sacc[1], qa[k][0], qa[k][1], b[2], b[3]);
         }
@@ -226,7 +235,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         for (int n = 0; n < NT; n += 2) {
           // matrices: (tok 0-7, d n*8..), (tok 8-15, d n*8..), (tok 0-7, d n*8+8..), (tok 8-15, d n*8+8..)
           uint32_t b[4];
-          ldsm_x4_trans(vbase + swz_off(p0 + (mi & 1) * 8 + mr, n + (mi >> 1), bs, sp.tile_stride), b);
+          ldsm_x4_trans(vrow + (uint32_t)((n >> 3) * hb_bytes) + (((((uint32_t)n & 7u) + vc) ^ vx) << 4), b);
           mma16816<T>(o[n], pa0, pa2, b[0], b[1]);
           mma16816<T>(o[n + 1], pa0, pa2, b[2], b[3]);
         }
@@ -259,7 +268,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
 }
 
 constexpr int kMmaNCW = 4;
-constexpr int kMmaRingTarget = 96 * 1024;
+constexpr int kMmaRingTarget = 64 * 1024;  // leaves room for 2 CTAs per SM
 
 template <typename T, int D>
 int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
