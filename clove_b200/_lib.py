@@ -54,6 +54,7 @@ SIGNATURES = {
     "clove_cuda_paged_decode": (_i, [_vp, _vp, _i, _vp, _i, _vp, _i, _f, _i, _vp, _vp, _sz, _vp]),
     "clove_cuda_paged_append_decode": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _i, _vp, _i, _f, _i, _vp, _vp,
                                             _sz, _vp]),
+    "clove_cuda_paged_append_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _i, _vp, _i, _f, _i, _vp, _vp]),
     "clove_cuda_decode_status": (_i, [_vp, _vp, _ip]),
     "clove_cuda_set_decode_variant": (_i, [_i]),
     "clove_cuda_launch_count": (C.c_uint64, []),

@@ -1,0 +1,100 @@
+// Append + decode without a caller-supplied workspace.
+//
+// Some callers cannot allocate device memory at the point where they decode:
+// an engine that has carved all of HBM into its KV pool up front, a host
+// runtime whose only device memory comes from a foreign allocator it may not
+// call on the serving path, or a plugin host that forbids cudaMalloc after
+// start-up.  clove_cuda_paged_append_decode_noalloc serves them: it runs the
+// same append + decode as clove_cuda_paged_append_decode, with its scratch in
+// a fixed array that this library places in every GPU's memory when the GPU
+// first loads it and keeps until the process exits.
+//
+// Limits and rules:
+//   - The scratch is kNoAllocScratchBytes (32 MiB) per GPU; calls whose
+//     workspace need (clove_cuda_decode_workspace_size) exceeds it are
+//     rejected with CLOVE_ERR_WORKSPACE.
+//   - Every call on a GPU shares the one array and it keeps what the last
+//     call left there; the plan kernel of each call re-initialises everything
+//     the decode reads from it (counters, item list, check flags).  Calls
+//     that overlap on the GPU (other streams, other host threads) race on it:
+//     serialise them.
+//   - The first call on a device looks up the array's device address (with
+//     that device current) and caches it; make that first call before any
+//     stream capture.
+#include <mutex>
+
+#include "host.h"
+
+namespace clove {
+
+constexpr size_t kNoAllocScratchBytes = 32u << 20;
+constexpr int kMaxDevices = 64;
+
+// The scratch.  In host code this name is only a stand-in for the symbol,
+// never a device address: kernels get the address from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static void* g_scratch_ptr[kMaxDevices] = {};
+static std::once_flag g_scratch_once[kMaxDevices];
+static cudaError_t g_scratch_err[kMaxDevices] = {};
+
+// Device address of the scratch on `device` (which must be current).
+static void* scratch_on(int device, cudaError_t* err) {
+  std::call_once(g_scratch_once[device], [device] {
+    void* p = nullptr;
+    g_scratch_err[device] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_scratch_ptr[device] = g_scratch_err[device] == cudaSuccess ? p : nullptr;
+  });
+  *err = g_scratch_err[device];
+  return g_scratch_ptr[device];
+}
+
+}  // namespace clove
+
+using namespace clove;
+
+extern "C" {
+
+int clove_cuda_paged_append_decode_noalloc(clove_pool_t pool, const void* q, const void* k_new,
+                                           const void* v_new, int num_q_heads, const int32_t* block_tables,
+                                           int bt_stride, const int32_t* context_lens, int batch, float scale,
+                                           int max_ctx, float* out, void* stream) {
+  if (!pool) {
+    set_last_error("paged_append_decode_noalloc: null pool");
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  if (pool->device < 0 || pool->device >= kMaxDevices) {
+    set_last_error("paged_append_decode_noalloc: device %d beyond %d", pool->device, kMaxDevices);
+    return CLOVE_ERR_NO_DEVICE;
+  }
+  if (batch <= 0 || num_q_heads <= 0 || max_ctx < 1) {
+    // Same argument checks (and messages) as the workspace entry point.
+    return clove_cuda_paged_append_decode(pool, q, k_new, v_new, num_q_heads, block_tables, bt_stride,
+                                          context_lens, batch, scale, max_ctx, out, nullptr, 0, stream);
+  }
+  const size_t need = clove_cuda_decode_workspace_size(pool, batch, num_q_heads, max_ctx);
+  if (need > kNoAllocScratchBytes) {
+    set_last_error(
+        "paged_append_decode_noalloc: this call needs %zu bytes of scratch, the built-in scratch holds %zu "
+        "(use clove_cuda_paged_append_decode with a workspace)",
+        need, kNoAllocScratchBytes);
+    return CLOVE_ERR_WORKSPACE;
+  }
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  if (prev != pool->device && cudaSetDevice(pool->device) != cudaSuccess) {
+    set_last_error("paged_append_decode_noalloc: cudaSetDevice(%d) failed", pool->device);
+    return CLOVE_ERR_CUDA;
+  }
+  cudaError_t e = cudaSuccess;
+  void* ws = scratch_on(pool->device, &e);
+  if (prev >= 0 && prev != pool->device) cudaSetDevice(prev);
+  if (!ws) {
+    set_last_error("paged_append_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    return CLOVE_ERR_CUDA;
+  }
+  return clove_cuda_paged_append_decode(pool, q, k_new, v_new, num_q_heads, block_tables, bt_stride, context_lens,
+                                        batch, scale, max_ctx, out, ws, kNoAllocScratchBytes, stream);
+}
+
+}  // extern "C"

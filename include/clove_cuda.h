@@ -164,6 +164,26 @@ int clove_cuda_paged_append_decode(clove_pool_t pool, const void* q,
                                    void* workspace, size_t workspace_bytes,
                                    void* stream);
 
+/* Append + decode for callers that cannot allocate device memory when they
+ * decode (an engine that hands all of HBM to its KV pool at start-up, a host
+ * whose device memory comes only from an allocator it may not call on the
+ * serving path).  No counterpart in the reference.  Same arguments and
+ * results as clove_cuda_paged_append_decode, minus the workspace: scratch
+ * comes from a fixed 32 MiB array the library keeps on every GPU that loads
+ * it, until the process exits.  Returns CLOVE_ERR_WORKSPACE when the call
+ * needs more than that (see clove_cuda_decode_workspace_size).  All calls on
+ * a GPU share the array: calls that overlap on the GPU race, so serialise
+ * them.  The first call on a device looks up the array's address; make it
+ * before any stream capture.  The call allocates nothing. */
+int clove_cuda_paged_append_decode_noalloc(clove_pool_t pool, const void* q,
+                                           const void* k_new, const void* v_new,
+                                           int num_q_heads,
+                                           const int32_t* block_tables,
+                                           int bt_stride,
+                                           const int32_t* context_lens,
+                                           int batch, float scale, int max_ctx,
+                                           float* out, void* stream);
+
 /* Synchronise `stream` and read the device check flags (CLOVE_FLAG_*) that
  * the most recent decode call on `workspace` raised (each call clears them
  * when it starts); the word is cleared after reading.  Returns
