@@ -145,6 +145,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Plain (non-tensor) bulk copy global -> shared; both addresses 16-byte
+// aligned and the size a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // Make this thread's generic-proxy global writes visible to later async-proxy
 // (TMA) reads.
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -200,6 +209,7 @@ struct DecodeArgs {
   int num_blocks;
   int block_size;
   const int32_t* chunk_blocks;  // device scalar: blocks per work item (set by the plan)
+  int32_t* unit_counter;        // work-claim counter (zeroed by the plan)
   int max_chunks;            // chunks per sequence, upper bound
   int max_ctx;
   int group;                 // query heads per KV head (runtime, <= template G)
@@ -224,6 +234,7 @@ struct PlanArgs {
   int min_chunk_blocks;      // lower bound on blocks per work item
   long long target_units;    // work units the chunk size aims for
   int32_t* chunk_blocks;     // out: blocks per work item chosen for this call
+  int32_t* unit_counter;     // zeroed: the decode kernel's work-claim counter
   int max_ctx;
   int append;
 };

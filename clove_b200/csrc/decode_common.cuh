@@ -42,28 +42,89 @@ __device__ __forceinline__ Unit load_unit(const DecodeArgs& a, int u, int sb) {
   return x;
 }
 
+// Units travel from the producer to the consumers through a small ring of
+// shared-memory slots (kUnitRing deep): the unit's metadata plus a copy of
+// its query rows, brought in by one bulk copy.  Consumers never touch global
+// memory at a unit boundary.
+constexpr int kUnitRing = 2;
+
+struct UnitSlot {
+  Unit x;
+  int nchunks;  // chunks of sequence x.b
+  int valid;    // 0: no more work
+};
+
 // Shared-memory carve-up: [ring: nstage x (K tiles | V tiles)] [barriers]
-// [scratch].  Every region starts 128-byte aligned (bulk tensor copies want
-// 128-byte aligned destinations).
+// [unit slots] [query buffers] [scratch].  Every region starts 128-byte
+// aligned (bulk tensor copies want 128-byte aligned destinations).
 struct SmemPlan {
   int tile_stride;   // bytes of one [block_size, head_dim] tile, 128-aligned
   int stage_bytes;   // 2 * sb tiles
   int ring_bytes;
-  int bar_bytes;
+  int bar_bytes;     // full/empty per stage, ufull/uempty per unit slot, misc ints
+  int slot_bytes;    // kUnitRing unit slots
+  int q_stride;      // bytes of one query buffer (group * head_dim elements max)
   int scratch_bytes;
   int total;         // + 128 alignment slack
 };
 
 __host__ __device__ inline SmemPlan smem_plan(int block_size, int head_dim, int elem_bytes, int sb, int nstage,
-                                             int scratch_bytes) {
+                                             int scratch_bytes, int q_bytes) {
   SmemPlan s;
   s.tile_stride = (block_size * head_dim * elem_bytes + 127) & ~127;
   s.stage_bytes = 2 * sb * s.tile_stride;
   s.ring_bytes = s.stage_bytes * nstage;
-  s.bar_bytes = ((2 * nstage * 8 + 64) + 127) & ~127;
+  s.bar_bytes = ((2 * nstage + 2 * kUnitRing) * 8 + 64 + 127) & ~127;
+  s.slot_bytes = (kUnitRing * (int)sizeof(UnitSlot) + 127) & ~127;
+  s.q_stride = (q_bytes + 127) & ~127;
   s.scratch_bytes = (scratch_bytes + 127) & ~127;
-  s.total = s.ring_bytes + s.bar_bytes + s.scratch_bytes + 128;
+  s.total = s.ring_bytes + s.bar_bytes + s.slot_bytes + kUnitRing * s.q_stride + s.scratch_bytes + 128;
   return s;
+}
+
+// Pointers into the carve-up, from the aligned base.
+struct SmemPtrs {
+  unsigned char* ring;
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* ufull;
+  uint64_t* uempty;
+  volatile int* misc;  // [0] abort, [1] last-CTA flag
+  UnitSlot* slots;
+  unsigned char* qbuf;  // kUnitRing x q_stride
+  float* scratch;
+};
+
+__device__ __forceinline__ SmemPtrs smem_ptrs(unsigned char* base, const SmemPlan& sp, int nstage) {
+  SmemPtrs p;
+  p.ring = base;
+  p.full = reinterpret_cast<uint64_t*>(base + sp.ring_bytes);
+  p.empty = p.full + nstage;
+  p.ufull = p.empty + nstage;
+  p.uempty = p.ufull + kUnitRing;
+  p.misc = reinterpret_cast<volatile int*>(p.uempty + kUnitRing);
+  p.slots = reinterpret_cast<UnitSlot*>(base + sp.ring_bytes + sp.bar_bytes);
+  p.qbuf = base + sp.ring_bytes + sp.bar_bytes + sp.slot_bytes;
+  p.scratch = reinterpret_cast<float*>(p.qbuf + kUnitRing * sp.q_stride);
+  return p;
+}
+
+// Barrier initialisation (thread 0), then a CTA barrier.
+__device__ __forceinline__ void init_barriers(const SmemPtrs& p, int nstage) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nstage; ++s) {
+      mbar_init(&p.full[s], 1);
+      mbar_init(&p.empty[s], 1);
+    }
+    for (int k = 0; k < kUnitRing; ++k) {
+      mbar_init(&p.ufull[k], 1);
+      mbar_init(&p.uempty[k], 1);
+    }
+    p.misc[0] = 0;
+    p.misc[1] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
 }
 
 // K tiles of a stage are at [0, sb) * tile_stride, V tiles at
@@ -98,63 +159,115 @@ __device__ __forceinline__ void append_row(const DecodeArgs& a, const Unit& x, i
   __syncwarp();
 }
 
-// The producer warp: walks the CTA's units and streams their K/V tiles into
-// the ring.  Only lane 0 issues copies; the warp loads block-table entries 32
-// at a time and broadcasts them.  On a stuck wait it raises the abort flag and
-// drains its own in-flight copies (bounded) before returning.
+// The producer warp.  It claims units from the plan's longest-first list
+// with an atomic counter, posts each one (metadata + a bulk copy of its query
+// rows) to the unit ring, performs the fused append when the unit holds the
+// sequence's last chunk, then streams the unit's K/V tiles into the stage
+// ring.  Halfway through a unit's stages (once the ring is primed) it claims
+// the next unit and loads its metadata and first block-table entries, so a
+// unit boundary costs no global round trip on the critical path.  Only lane
+// 0 issues copies.  On a stuck wait it raises the abort flag and drains its
+// own in-flight copies (bounded) before returning.
 //
 // NBOX: boxes per tile.  1 = one [block_size, head_dim] box (dense rows);
 // D/64 = head_dim split into 64-element (128-byte) boxes written with the
 // 128-byte swizzle, sub-tile hb at tile offset hb * block_size * 128.
 template <typename T, int D, int NBOX>
-__device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
-                        unsigned char* ring, const SmemPlan& sp, int sb, uint64_t* full, uint64_t* empty,
-                        volatile int* s_abort, int n_units) {
+__device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUtensorMap* tm_v, const SmemPtrs& sm,
+                        const SmemPlan& sp, int sb, int n_units) {
   const int lane = threadIdx.x & 31;
   const int bs = a.block_size;
   const uint32_t tile_bytes = (uint32_t)(bs * D * (int)sizeof(T));
+  const uint32_t q_bytes = (uint32_t)(a.group * D * (int)sizeof(T));
+  const int Hq = a.num_kv_heads * a.group;
   const uint64_t pol = policy_evict_first();
-  int slot = 0;
-  uint32_t phase = 0;
+  int slot = 0, uk = 0;
+  uint32_t phase = 0, uphase = 0;
   bool aborted = false;
-  for (int u = blockIdx.x; u < n_units && !aborted; u += gridDim.x) {
-    const Unit x = load_unit(a, u, sb);
+
+  // Block-table entries, 32 at a time (lane i holds entry j0 + i); entries
+  // outside the pool are flagged and replaced by block 0 (never followed).
+  auto table = [&](const Unit& x, int j0) {
+    const bool in = j0 + lane < x.nblk;
+    int v = in ? __ldg(a.block_tables + (size_t)x.b * a.bt_stride + x.blk0 + j0 + lane) : 0;
+    if (in && (v < 0 || v >= a.num_blocks)) {
+      atomicOr(a.err, CLOVE_FLAG_BLOCK_OOB);
+      v = 0;
+    }
+    return v;
+  };
+  auto claim = [&](int& u, Unit& x, int& bt0) {
+    int v = 0;
+    if (lane == 0) v = atomicAdd(a.unit_counter, 1);
+    u = __shfl_sync(0xffffffffu, v, 0);
+    if (u < n_units) {
+      x = load_unit(a, u, sb);
+      bt0 = table(x, 0);
+    }
+  };
+
+  int u, bt0 = 0;
+  Unit x;
+  claim(u, x, bt0);
+  while (!aborted) {
+    // ---- post the unit (or the end marker) to the unit ring ----
+    int ok = 1;
+    if (lane == 0) {
+      if (*sm.misc || !mbar_wait_bounded(&sm.uempty[uk], uphase ^ 1, a.err)) {
+        ok = 0;
+        *sm.misc = 1;
+      } else if (u >= n_units) {
+        sm.slots[uk].valid = 0;
+        mbar_arrive(&sm.ufull[uk]);
+      } else {
+        sm.slots[uk].x = x;
+        sm.slots[uk].nchunks = a.seq_chunks[x.b];
+        sm.slots[uk].valid = 1;
+        mbar_arrive_expect_tx(&sm.ufull[uk], q_bytes);
+        const T* qsrc = static_cast<const T*>(a.q) + ((size_t)x.b * Hq + (size_t)x.h * a.group) * D;
+        bulk_load(sm.qbuf + uk * sp.q_stride, qsrc, q_bytes, &sm.ufull[uk]);
+      }
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) {
+      aborted = true;
+      break;
+    }
+    if (u >= n_units) break;
+    if (++uk == kUnitRing) {
+      uk = 0;
+      uphase ^= 1;
+    }
+
     if (a.append && x.c == a.seq_chunks[x.b] - 1) append_row<T, D>(a, x, lane);
-    const int32_t* bt = a.block_tables + (size_t)x.b * a.bt_stride + x.blk0;
-    int my = 0;
+    int my = bt0;
+    int u2 = n_units, bt2 = 0;
+    Unit x2;
+    const int claim_at = min(x.nstages - 1, a.nstage / 2);
     for (int s = 0; s < x.nstages && !aborted; ++s) {
       const int j0 = s * sb;  // first block of this stage within the chunk
-      if ((j0 & 31) == 0) {
-        my = 0;
-        if (j0 + lane < x.nblk) {
-          my = __ldg(bt + j0 + lane);
-          if (my < 0 || my >= a.num_blocks) {
-            atomicOr(a.err, CLOVE_FLAG_BLOCK_OOB);
-            my = 0;
-          }
-        }
-      }
+      if ((j0 & 31) == 0 && j0 > 0) my = table(x, j0);
       const int nb = min(sb, x.nblk - j0);
-      int ok = 1;
       int phys[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) phys[i] = __shfl_sync(0xffffffffu, my, (j0 + i) & 31);
+      ok = 1;
       if (lane == 0) {
-        if (*s_abort || !mbar_wait_bounded(&empty[slot], phase ^ 1, a.err)) {
+        if (*sm.misc || !mbar_wait_bounded(&sm.empty[slot], phase ^ 1, a.err)) {
           ok = 0;
-          *s_abort = 1;
+          *sm.misc = 1;
         } else {
-          mbar_arrive_expect_tx(&full[slot], 2u * tile_bytes * (uint32_t)nb);
-          unsigned char* st = ring + (size_t)slot * sp.stage_bytes;
+          mbar_arrive_expect_tx(&sm.full[slot], 2u * tile_bytes * (uint32_t)nb);
+          unsigned char* st = sm.ring + (size_t)slot * sp.stage_bytes;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             if (i < nb) {
 #pragma unroll
               for (int hb = 0; hb < NBOX; ++hb) {
                 const int off = hb * (D / NBOX) * (int)sizeof(T) * bs;
-                tma_load_3d(st + i * sp.tile_stride + off, tm_k, &full[slot], hb * (D / NBOX), x.h, phys[i] * bs,
+                tma_load_3d(st + i * sp.tile_stride + off, tm_k, &sm.full[slot], hb * (D / NBOX), x.h, phys[i] * bs,
                             pol);
-                tma_load_3d(st + (sb + i) * sp.tile_stride + off, tm_v, &full[slot], hb * (D / NBOX), x.h,
+                tma_load_3d(st + (sb + i) * sp.tile_stride + off, tm_v, &sm.full[slot], hb * (D / NBOX), x.h,
                             phys[i] * bs, pol);
               }
             }
@@ -167,10 +280,15 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
         slot = 0;
         phase ^= 1;
       }
+      if (s == claim_at) claim(u2, x2, bt2);
     }
+    u = u2;
+    x = x2;
+    bt0 = bt2;
   }
   if (aborted && lane == 0) {
-    // Drain: the last nstage issues may still be in flight.
+    // Drain: the last nstage stage issues and the last unit-slot posts may
+    // still be in flight.
     int s = slot;
     uint32_t ph = phase;
     for (int k = 0; k < a.nstage; ++k) {
@@ -179,9 +297,32 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
         ph ^= 1;
       }
       for (uint32_t i = 0; i < kWaitLimit; ++i)
-        if (mbar_try_wait(&full[s], ph)) break;
+        if (mbar_try_wait(&sm.full[s], ph)) break;
+    }
+    int k2 = uk;
+    uint32_t uph = uphase;
+    for (int k = 0; k < kUnitRing; ++k) {
+      if (--k2 < 0) {
+        k2 = kUnitRing - 1;
+        uph ^= 1;
+      }
+      for (uint32_t i = 0; i < kWaitLimit; ++i)
+        if (mbar_try_wait(&sm.ufull[k2], uph)) break;
     }
   }
+}
+
+// Consumer side of the unit ring: wait for the next posted unit.  Returns
+// false when the kernel must stop (end marker, or a stuck wait anywhere —
+// all NCT consumer threads agree through the barrier reduction).
+template <int NCT>
+__device__ __forceinline__ bool next_unit(const DecodeArgs& a, const SmemPtrs& sm, int uk, uint32_t uphase,
+                                          UnitSlot& out) {
+  const bool ok = !sm.misc[0] && mbar_wait_bounded(&sm.ufull[uk], uphase, a.err);
+  if (!ok) sm.misc[0] = 1;
+  if (named_bar_or(1, NCT, ok ? 0 : 1)) return false;
+  out = sm.slots[uk];
+  return out.valid != 0;
 }
 
 // Epilogue of one unit, run by all NCT consumer threads (ct in [0, NCT)).
@@ -191,12 +332,11 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
 // the last chunk of (b, h) — found with an atomic counter, no waiting —
 // merges all chunks and writes the output.
 template <int D, int G, int NW, int NCT>
-__device__ void finish_unit(const DecodeArgs& a, const Unit& x, const float* scratch, volatile int* s_last,
-                            int ct) {
+__device__ void finish_unit(const DecodeArgs& a, const Unit& x, int nchunks, const float* scratch,
+                            volatile int* s_last, int ct) {
   const int group = a.group;
   const int Hkv = a.num_kv_heads;
   const int Hq = Hkv * group;
-  const int nchunks = a.seq_chunks[x.b];
   float* part_base = a.partials + (((size_t)x.b * Hkv + x.h) * a.max_chunks) * G * (D + 2);
   for (int idx = ct; idx < group * D; idx += NCT) {
     const int g = idx / D, d = idx - (idx / D) * D;

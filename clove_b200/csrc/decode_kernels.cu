@@ -45,16 +45,55 @@ namespace clove {
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
 
+constexpr int kPlanBins = 256;
+
+// Block-wide exclusive scan of one int per thread; *total gets the sum.
+__device__ __forceinline__ int block_excl_scan(int n, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = n;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_tot[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  const int excl = x - n + (warp > 0 ? warp_tot[warp - 1] : 0);
+  *total = warp_tot[31];
+  __syncthreads();
+  return excl;
+}
+
+// Work list, longest first: every sequence of nbl blocks yields nbl / cb
+// full chunks (listed first, all the same size) and, if nbl % cb != 0, one
+// partial chunk; the partial chunks follow in descending size order (counting
+// sort over kPlanBins size bins).  The decode kernel's CTAs claim units from
+// the front with an atomic counter, so the big units start first and the
+// small ones fill the tail.
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
   __shared__ int warp_tot[32];
-  __shared__ int s_base;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ int hist[kPlanBins];
+  __shared__ int binbase[kPlanBins];
   __shared__ long long s_blocks;
+  __shared__ int s_full;
+  const int tid = threadIdx.x, lane = tid & 31;
   if (tid == 0) {
-    s_base = 0;
     s_blocks = 0;
-    *p.err = 0;  // flags report the most recent call only
+    s_full = 0;
+    *p.err = 0;            // flags report the most recent call only
+    *p.unit_counter = 0;   // the decode kernel's work-claim counter
   }
+  for (int i = tid; i < kPlanBins; i += kPlanThreads) hist[i] = 0;
   __syncthreads();
   // Chunk size from the actual work: total (block, KV head) pairs spread
   // over ~target_units work items, never below min_chunk_blocks.
@@ -70,50 +109,55 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
   __syncthreads();
   const long long want = (s_blocks * p.num_kv_heads + p.target_units - 1) / p.target_units;
   const int cb = (int)max((long long)p.min_chunk_blocks, want);
-  const int chunk_tokens = cb * p.block_size;
   if (tid == 0) *p.chunk_blocks = cb;
+
+  // pass 1: per-sequence bookkeeping, full chunks, partial-size histogram
   for (int base = 0; base < p.batch; base += kPlanThreads) {
     const int b = base + tid;
-    int n = 0;
+    int nfull = 0;
     if (b < p.batch) {
-      int raw = p.context_lens[b];
-      int L = clamp_ctx(p.context_lens, b, p.max_ctx, p.append);
+      const int raw = p.context_lens[b];
+      const int L = clamp_ctx(p.context_lens, b, p.max_ctx, p.append);
       if (raw != L - p.append) atomicOr(p.err, CLOVE_FLAG_CTX_RANGE);
-      n = (L + chunk_tokens - 1) / chunk_tokens;
-      p.seq_chunks[b] = n;
+      const int nbl = (L + p.block_size - 1) / p.block_size;
+      nfull = nbl / cb;
+      const int rem = nbl - nfull * cb;
+      p.seq_chunks[b] = nfull + (rem > 0);
       for (int h = 0; h < p.num_kv_heads; ++h) p.counters[(size_t)b * p.num_kv_heads + h] = 0;
+      if (rem > 0) atomicAdd(&hist[(rem - 1) * kPlanBins / cb], 1);
       if (L == 0) {
         float* row = p.out + (size_t)b * p.row_floats;
         for (int i = 0; i < p.row_floats; ++i) row[i] = 0.f;
       }
     }
-    // block-wide exclusive scan of n
-    int x = n;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) warp_tot[warp] = x;
+    int tot;
+    const int excl = block_excl_scan(nfull, warp_tot, &tot);
+    for (int c = 0; c < nfull; ++c) p.items[s_full + excl + c] = make_int2(b, c);
     __syncthreads();
-    if (warp == 0) {
-      int w = warp_tot[lane];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        int y = __shfl_up_sync(0xffffffffu, w, o);
-        if (lane >= o) w += y;
-      }
-      warp_tot[lane] = w;  // inclusive over warps
-    }
-    __syncthreads();
-    int excl = x - n + (warp > 0 ? warp_tot[warp - 1] : 0);
-    int off = s_base + excl;
-    for (int c = 0; c < n; ++c) p.items[off + c] = make_int2(b, c);
-    __syncthreads();
-    if (tid == 0) s_base += warp_tot[31];
+    if (tid == 0) s_full += tot;
     __syncthreads();
   }
-  if (tid == 0) *p.n_items = s_base;
+  // partial chunks: bases per size bin, largest bin first
+  if (tid == 0) {
+    int acc = s_full;
+    for (int bin = kPlanBins - 1; bin >= 0; --bin) {
+      binbase[bin] = acc;
+      acc += hist[bin];
+      hist[bin] = 0;  // reused as the per-bin cursor
+    }
+    *p.n_items = acc;
+  }
+  __syncthreads();
+  for (int b = tid; b < p.batch; b += kPlanThreads) {
+    const int L = clamp_ctx(p.context_lens, b, p.max_ctx, p.append);
+    const int nbl = (L + p.block_size - 1) / p.block_size;
+    const int nfull = nbl / cb;
+    const int rem = nbl - nfull * cb;
+    if (rem > 0) {
+      const int bin = (rem - 1) * kPlanBins / cb;
+      p.items[binbase[bin] + atomicAdd(&hist[bin], 1)] = make_int2(b, nfull);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -157,30 +201,17 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  const SmemPlan sp =
-      smem_plan(bs, D, (int)sizeof(T), sb, a.nstage, (NCW * G * (D + 2) + G * D) * (int)sizeof(float));
-  unsigned char* ring = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.ring_bytes);
-  uint64_t* empty = full + a.nstage;
-  volatile int* s_misc = reinterpret_cast<volatile int*>(empty + a.nstage);  // [0] abort, [1] last
-  float* scratch = reinterpret_cast<float*>(smem + sp.ring_bytes + sp.bar_bytes);
+  const SmemPlan sp = smem_plan(bs, D, (int)sizeof(T), sb, a.nstage,
+                                (NCW * G * (D + 2) + G * D) * (int)sizeof(float), G * D * (int)sizeof(T));
+  const SmemPtrs sm = smem_ptrs(smem, sp, a.nstage);
+  float* scratch = sm.scratch;
   float* qs = scratch + NCW * G * (D + 2);
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < a.nstage; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    s_misc[0] = 0;
-    s_misc[1] = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
+  init_barriers(sm, a.nstage);
   const int n_units = *a.n_items * a.num_kv_heads;
 
   if (warp == 0) {
-    produce<T, D, 1>(a, &tm_k, &tm_v, ring, sp, sb, full, empty, &s_misc[0], n_units);
+    produce<T, D, 1>(a, &tm_k, &tm_v, sm, sp, sb, n_units);
     return;
   }
 
@@ -190,11 +221,14 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   const int part = lane % LPT;    // which D/LPT slice of that token
   int gbase = 0;                  // stages of earlier units (CTA-wide count)
   float* my_scr = scratch + (size_t)cw * G * (D + 2);
+  int uk = 0;
+  uint32_t uphase = 0;
+  UnitSlot us;
 
-  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-    const Unit x = load_unit(a, u, sb);
+  while (next_unit<NCT>(a, sm, uk, uphase, us)) {
+    const Unit x = us.x;
     {
-      const T* qg = static_cast<const T*>(a.q) + ((size_t)x.b * Hq + (size_t)x.h * group) * D;
+      const T* qg = reinterpret_cast<const T*>(sm.qbuf + uk * sp.q_stride);
       for (int i = ct; i < group * D; i += NCT) qs[i] = Elem<T>::to_f(qg[i]) * a.qscale;
     }
     named_bar_sync(1, NCT);
@@ -218,13 +252,13 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       const int gs = gbase + j;
       const int slot = gs % a.nstage;
       const uint32_t par = (uint32_t)(gs / a.nstage) & 1u;
-      if (s_misc[0] || !mbar_wait_bounded(&full[slot], par, a.err)) {
-        s_misc[0] = 1;
+      if (sm.misc[0] || !mbar_wait_bounded(&sm.full[slot], par, a.err)) {
+        sm.misc[0] = 1;
         aborted = true;
         break;
       }
-      const T* Ks = reinterpret_cast<const T*>(ring + (size_t)slot * sp.stage_bytes);
-      const T* Vs = reinterpret_cast<const T*>(ring + (size_t)slot * sp.stage_bytes + sb * sp.tile_stride);
+      const T* Ks = reinterpret_cast<const T*>(sm.ring + (size_t)slot * sp.stage_bytes);
+      const T* Vs = reinterpret_cast<const T*>(sm.ring + (size_t)slot * sp.stage_bytes + sb * sp.tile_stride);
       const int ntok = min(TT, x.L - (x.blk0 + j * sb) * bs);
       for (int p0 = 0; p0 < ntok; p0 += P) {
         const int tk = p0 + tk_l;
@@ -290,7 +324,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (lane == 0) mbar_arrive(&sm.empty[slot]);
     }
     // A consumer warp that met a stuck wait stops here; the reduction keeps
     // every consumer thread on the same path (no one is left at a barrier).
@@ -309,8 +343,13 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       }
     }
     named_bar_sync(1, NCT);
-    finish_unit<D, G, NCW, NCT>(a, x, scratch, &s_misc[1], ct);
-    named_bar_sync(1, NCT);  // scratch, q and s_misc[1] are reused by the next unit
+    finish_unit<D, G, NCW, NCT>(a, x, us.nchunks, scratch, &sm.misc[1], ct);
+    named_bar_sync(1, NCT);  // scratch, q and misc[1] are reused by the next unit
+    if (ct == 0) mbar_arrive(&sm.uempty[uk]);
+    if (++uk == kUnitRing) {
+      uk = 0;
+      uphase ^= 1;
+    }
   }
 }
 
@@ -359,21 +398,22 @@ static int run_simt(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) 
   const int bs = pool.block_size;
   const int sb = bs >= 16 ? 1 : 16 / bs;
   const int scratch = (kNCW * G * (D + 2) + G * D) * 4;
-  SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch);
+  const int qb = G * D * (int)sizeof(T);
+  SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb);
   // nstage: a multiple of the number of consumer warps that take stages (see
   // the kernel); large tiles use fewer of them.
   int ncw = kNCW;
   int nstage = (kRingTarget / sp.stage_bytes) / ncw * ncw;
   if (nstage < ncw) nstage = ncw;
   if (nstage > 4 * ncw) nstage = 4 * ncw;
-  sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch);
+  sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);
   while (sp.total > 200 * 1024 && nstage > 1) {
     if (nstage > ncw) {
       nstage -= ncw;
     } else {
       ncw = --nstage;
     }
-    sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch);
+    sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);
   }
   a.ncw = ncw;
   if (sp.total > 227 * 1024) {
@@ -461,6 +501,7 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   p.min_chunk_blocks = L.chunk_blocks;
   p.target_units = (long long)pool.num_sms * 8;  // ~4 units per resident CTA at 2 CTAs/SM
   p.chunk_blocks = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 1;
+  p.unit_counter = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 2;
   p.max_ctx = call.max_ctx;
   p.append = append;
   plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
@@ -492,6 +533,7 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   a.num_blocks = pool.num_blocks;
   a.block_size = pool.block_size;
   a.chunk_blocks = p.chunk_blocks;
+  a.unit_counter = p.unit_counter;
   a.max_chunks = L.max_chunks;
   a.max_ctx = call.max_ctx;
   a.group = call.num_q_heads / pool.num_kv_heads;

@@ -104,28 +104,15 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const SmemPlan sp = smem_plan(bs, D, (int)sizeof(T), sb, a.nstage, NCW * G * (D + 2) * (int)sizeof(float));
-  unsigned char* ring = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.ring_bytes);
-  uint64_t* empty = full + a.nstage;
-  volatile int* s_misc = reinterpret_cast<volatile int*>(empty + a.nstage);
-  float* scratch = reinterpret_cast<float*>(smem + sp.ring_bytes + sp.bar_bytes);
-
+  const SmemPlan sp = smem_plan(bs, D, (int)sizeof(T), sb, a.nstage, NCW * G * (D + 2) * (int)sizeof(float),
+                                G * D * (int)sizeof(T));
+  const SmemPtrs sm = smem_ptrs(smem, sp, a.nstage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < a.nstage; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    s_misc[0] = 0;
-    s_misc[1] = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
+  init_barriers(sm, a.nstage);
   const int n_units = *a.n_items * a.num_kv_heads;
 
   if (warp == 0) {
-    produce<T, D, D / 64>(a, &tm_k, &tm_v, ring, sp, sb, full, empty, &s_misc[0], n_units);
+    produce<T, D, D / 64>(a, &tm_k, &tm_v, sm, sp, sb, n_units);
     return;
   }
 
@@ -137,14 +124,18 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   const int mr = lane & 7;      // ldmatrix: which row of it
   const float sl2 = a.qscale;   // scale * log2(e), applied to the f32 scores
   int gbase = 0;
-  float* my_scr = scratch + (size_t)cw * G * (D + 2);
+  float* my_scr = sm.scratch + (size_t)cw * G * (D + 2);
+  int uk = 0;
+  uint32_t uphase = 0;
+  UnitSlot us;
 
-  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-    const Unit x = load_unit(a, u, sb);
-    // Q fragments (A operand rows = query heads of this KV head), unscaled.
+  while (next_unit<NCT>(a, sm, uk, uphase, us)) {
+    const Unit x = us.x;
+    // Q fragments (A operand rows = query heads of this KV head), unscaled,
+    // from the unit's query buffer.
     uint32_t qa[KS][2];
     {
-      const T* qrow = static_cast<const T*>(a.q) + ((size_t)x.b * Hq + (size_t)x.h * group + g) * D;
+      const T* qrow = reinterpret_cast<const T*>(sm.qbuf + uk * sp.q_stride) + g * D;
 #pragma unroll
       for (int k = 0; k < KS; ++k) {
         if (g < group) {
@@ -168,12 +159,12 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       const int gs = gbase + j;
       const int slot = gs % a.nstage;
       const uint32_t par = (uint32_t)(gs / a.nstage) & 1u;
-      if (s_misc[0] || !mbar_wait_bounded(&full[slot], par, a.err)) {
-        s_misc[0] = 1;
+      if (sm.misc[0] || !mbar_wait_bounded(&sm.full[slot], par, a.err)) {
+        sm.misc[0] = 1;
         aborted = true;
         break;
       }
-      unsigned char* kst = ring + (size_t)slot * sp.stage_bytes;
+      unsigned char* kst = sm.ring + (size_t)slot * sp.stage_bytes;
       unsigned char* vst = kst + sb * sp.tile_stride;
       const int ntok = min(TT, x.L - (x.blk0 + j * sb) * bs);
       if (ntok < TT) {
@@ -242,7 +233,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       }
       if (ntok < TT) fence_proxy_async_smem();  // order the zero-fill before the slot's next bulk copy
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (lane == 0) mbar_arrive(&sm.empty[slot]);
     }
     if (named_bar_or(1, NCT, aborted ? 1 : 0)) return;
     gbase += x.nstages;
@@ -262,8 +253,13 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       }
     }
     named_bar_sync(1, NCT);
-    finish_unit<D, G, NCW, NCT>(a, x, scratch, &s_misc[1], ct);
+    finish_unit<D, G, NCW, NCT>(a, x, us.nchunks, sm.scratch, &sm.misc[1], ct);
     named_bar_sync(1, NCT);
+    if (ct == 0) mbar_arrive(&sm.uempty[uk]);
+    if (++uk == kUnitRing) {
+      uk = 0;
+      uphase ^= 1;
+    }
   }
 }
 
@@ -280,19 +276,20 @@ int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
   const int bs = pool.block_size;
   const int sb = bs >= 16 ? 1 : 16 / bs;
   const int scratch = kMmaNCW * 8 * (D + 2) * 4;
-  SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch);
+  const int qb = 8 * D * (int)sizeof(T);
+  SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb);
   int ncw = kMmaNCW;
   int nstage = (kMmaRingTarget / sp.stage_bytes) / ncw * ncw;
   if (nstage < ncw) nstage = ncw;
   if (nstage > 4 * ncw) nstage = 4 * ncw;
-  sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch);
+  sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);
   while (sp.total + 1024 > 200 * 1024 && nstage > 1) {
     if (nstage > ncw) {
       nstage -= ncw;
     } else {
       ncw = --nstage;
     }
-    sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch);
+    sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);
   }
   const int smem = sp.total + 1024;  // 1024-byte alignment slack for the swizzled ring
   if (smem > 227 * 1024) {
