@@ -216,6 +216,7 @@ struct DecodeArgs {
   int append;                // 1: context_lens are pre-append lengths
   int nstage;                // pipeline depth (a multiple of ncw)
   int ncw;                   // consumer warps that take stages (<= the kernel's NCW)
+  int stage_blocks;          // blocks per pipeline stage (1..4)
   float qscale;              // scale * log2(e)
 };
 

@@ -189,7 +189,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   constexpr int NCT = NCW * 32;
   constexpr int EPC = 16 / (int)sizeof(T);  // elements per 16-byte chunk
   const int bs = a.block_size;
-  const int sb = bs >= 16 ? 1 : 16 / bs;
+  const int sb = a.stage_blocks;
   const int TT = sb * bs;
   const int P = TT < 32 ? TT : 32;
   const int LPT = 32 / P;
@@ -397,6 +397,7 @@ static int run_simt(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) 
   auto kern = paged_decode_simt_kernel<T, D, G, kNCW>;
   const int bs = pool.block_size;
   const int sb = bs >= 16 ? 1 : 16 / bs;
+  a.stage_blocks = sb;
   const int scratch = (kNCW * G * (D + 2) + G * D) * 4;
   const int qb = G * D * (int)sizeof(T);
   SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb);

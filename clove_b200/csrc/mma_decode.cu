@@ -96,7 +96,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   constexpr int NT = D / 8;         // n-tiles of P.V
   constexpr int NCT = NCW * 32;
   const int bs = a.block_size;
-  const int sb = bs >= 16 ? 1 : 16 / bs;
+  const int sb = a.stage_blocks;
   const int TT = sb * bs;
   const int group = a.group;
   const int Hq = a.num_kv_heads * group;
@@ -274,7 +274,10 @@ int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
   }
   auto kern = paged_decode_mma_kernel<T, D, kMmaNCW>;
   const int bs = pool.block_size;
-  const int sb = bs >= 16 ? 1 : 16 / bs;
+  // Stages of >= 32 tokens: fixed per-stage costs (barrier round trips, copy
+  // issue) halve against 16-token stages.
+  const int sb = bs >= 32 ? 1 : 32 / bs;
+  a.stage_blocks = sb;
   const int scratch = kMmaNCW * 8 * (D + 2) * 4;
   const int qb = 8 * D * (int)sizeof(T);
   SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb);
