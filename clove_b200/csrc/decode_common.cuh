@@ -337,7 +337,9 @@ __device__ void finish_unit(const DecodeArgs& a, const Unit& x, int nchunks, con
   const int group = a.group;
   const int Hkv = a.num_kv_heads;
   const int Hq = Hkv * group;
-  float* part_base = a.partials + (((size_t)x.b * Hkv + x.h) * a.max_chunks) * G * (D + 2);
+  // Partials [B*Hkv, max_chunks, group, D + 2], indexed by the runtime group
+  // (the workspace is sized by it, not by the kernel's row capacity G).
+  float* part_base = a.partials + (((size_t)x.b * Hkv + x.h) * a.max_chunks) * group * (D + 2);
   for (int idx = ct; idx < group * D; idx += NCT) {
     const int g = idx / D, d = idx - (idx / D) * D;
     float M = -INFINITY;
@@ -356,7 +358,7 @@ __device__ void finish_unit(const DecodeArgs& a, const Unit& x, int nchunks, con
     if (nchunks == 1) {
       a.out[((size_t)x.b * Hq + (size_t)x.h * group + g) * D + d] = O / Ls;
     } else {
-      float* P = part_base + ((size_t)x.c * G + g) * (D + 2);
+      float* P = part_base + ((size_t)x.c * group + g) * (D + 2);
       P[d] = O;
       if (d == 0) {
         P[D] = M;
@@ -378,10 +380,10 @@ __device__ void finish_unit(const DecodeArgs& a, const Unit& x, int nchunks, con
         const int g = idx / D, d = idx - (idx / D) * D;
         float M = -INFINITY;
         for (int cc = 0; cc < nchunks; ++cc)
-          M = fmaxf(M, __ldcg(part_base + ((size_t)cc * G + g) * (D + 2) + D));
+          M = fmaxf(M, __ldcg(part_base + ((size_t)cc * group + g) * (D + 2) + D));
         float Ls = 0.f, O = 0.f;
         for (int cc = 0; cc < nchunks; ++cc) {
-          const float* P = part_base + ((size_t)cc * G + g) * (D + 2);
+          const float* P = part_base + ((size_t)cc * group + g) * (D + 2);
           const float f = exp2f(__ldcg(P + D) - M);
           Ls = fmaf(__ldcg(P + D + 1), f, Ls);
           O = fmaf(__ldcg(P + d), f, O);

@@ -386,8 +386,8 @@ DecodeLayout decode_layout(const clove_pool& pool, int batch, int num_q_heads, i
   off = align256(off + sizeof(int32_t) * (size_t)batch * hkv);
   L.off_partials = off;
   // Partials are only written when a sequence spans more than one chunk.
-  const size_t gpad = group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : group <= 8 ? 8 : 16;
-  if (L.max_chunks > 1) off = align256(off + sizeof(float) * (size_t)batch * hkv * L.max_chunks * gpad * (pool.head_dim + 2));
+  if (L.max_chunks > 1)
+    off = align256(off + sizeof(float) * (size_t)batch * hkv * L.max_chunks * group * (pool.head_dim + 2));
   L.total = off;
   return L;
 }

@@ -24,6 +24,8 @@
 #include "host.h"
 #include "mma_decode.cuh"
 
+#include <cstdlib>
+
 namespace clove {
 
 template <typename T> struct MmaType;
@@ -40,23 +42,27 @@ template <> struct MmaType<__half> {
   }
 };
 
-// D(16x8, f32) += A(16x16) * B(16x8); A rows 8..15 are zero (registers a1,
-// a3 = 0), so only d0, d1 (row lane/4) carry results; d2, d3 stay zero.
+// D(16x8, f32) += A(16x16) * B(16x8) with A rows 8..15 zero (registers a1,
+// a3 = 0): only d0, d1 (row lane/4) carry results, so the accumulator is the
+// pair (d0, d1); the zero rows are fed in as constants and their outputs
+// discarded.
 template <typename T>
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma16816(float (&d)[2], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
   const uint32_t z = 0;
+  const float zf = 0.f;
+  float x2, x3;
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+        "{%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(x2), "=f"(x3)
+        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1), "f"(d[0]), "f"(d[1]), "f"(zf), "f"(zf));
   } else {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+        "{%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(x2), "=f"(x3)
+        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1), "f"(d[0]), "f"(d[1]), "f"(zf), "f"(zf));
   }
 }
 
@@ -148,9 +154,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       }
     }
     float m = -INFINITY, l = 0.f;
-    float o[NT][4];
+    float o[NT][2];
 #pragma unroll
-    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = 0.f;
 
     bool aborted = false;
     const int ncw = a.ncw;
@@ -178,57 +184,83 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       }
       const uint32_t kbase = smem_u32(kst), vbase = smem_u32(vst);
       const int hb_bytes = bs * 128;  // one 64-dim sub-tile
-      for (int p0 = 0; p0 < ntok; p0 += 16) {
-        // Per-pass ldmatrix row addresses: chunk ch of token tok lives at
+      for (int p0 = 0; p0 < ntok; p0 += 32) {
+        // 32 tokens per pass, as two 16-token halves h = 0, 1.  Per-pass
+        // ldmatrix row addresses: chunk ch of token tok lives at
         // row_off(tok) + (ch >> 3) * hb_bytes + (((ch & 7) ^ (tok_row & 7)) << 4).
-        const int tk_k = p0 + (mi >> 1) * 8 + mr, tk_v = p0 + (mi & 1) * 8 + mr;
-        const int bk = tk_k / bs, rk = tk_k - bk * bs;
-        const int bv = tk_v / bs, rv = tk_v - bv * bs;
-        const uint32_t krow = kbase + (uint32_t)(bk * sp.tile_stride + rk * 128), kx = (uint32_t)(rk & 7);
-        const uint32_t vrow = vbase + (uint32_t)(bv * sp.tile_stride + rv * 128), vx = (uint32_t)(rv & 7);
+        uint32_t krow[2], kx[2], vrow[2], vx[2];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int tk_k = p0 + 16 * h2 + (mi >> 1) * 8 + mr, tk_v = p0 + 16 * h2 + (mi & 1) * 8 + mr;
+          const int bk = tk_k / bs, rk = tk_k - bk * bs;
+          const int bv = tk_v / bs, rv = tk_v - bv * bs;
+          krow[h2] = kbase + (uint32_t)(bk * sp.tile_stride + rk * 128);
+          kx[h2] = (uint32_t)(rk & 7);
+          vrow[h2] = vbase + (uint32_t)(bv * sp.tile_stride + rv * 128);
+          vx[h2] = (uint32_t)(rv & 7);
+        }
         const uint32_t kc = (uint32_t)(mi & 1), vc = (uint32_t)(mi >> 1);
-        // ---- S = Q K^T for tokens p0 .. p0+15 ----
-        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        // ---- S = Q K^T: 4 n-tiles of 8 tokens, 4 independent MMA chains ----
+        float sacc[4][2];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sacc[j][0] = sacc[j][1] = 0.f;
 #pragma unroll
         for (int k = 0; k < KS; ++k) {
+          const uint32_t off = (uint32_t)((k >> 2) * hb_bytes);
           // matrices: (tok 0-7, d 0-7), (tok 0-7, d 8-15), (tok 8-15, d 0-7), (tok 8-15, d 8-15)
-          uint32_t b[4];
-          ldsm_x4(krow + (uint32_t)((k >> 2) * hb_bytes) + (((((uint32_t)(2 * k) & 7u) + kc) ^ kx) << 4), b);
-          mma16816<T>(sacc[0], qa[k][0], qa[k][1], b[0], b[1]);
-          mma16816<T>(sacc[1], qa[k][0], qa[k][1], b[2], b[3]);
+          uint32_t b0[4], b1[4];
+          ldsm_x4(krow[0] + off + (((((uint32_t)(2 * k) & 7u) + kc) ^ kx[0]) << 4), b0);
+          ldsm_x4(krow[1] + off + (((((uint32_t)(2 * k) & 7u) + kc) ^ kx[1]) << 4), b1);
+          mma16816<T>(sacc[0], qa[k][0], qa[k][1], b0[0], b0[1]);
+          mma16816<T>(sacc[1], qa[k][0], qa[k][1], b0[2], b0[3]);
+          mma16816<T>(sacc[2], qa[k][0], qa[k][1], b1[0], b1[1]);
+          mma16816<T>(sacc[3], qa[k][0], qa[k][1], b1[2], b1[3]);
         }
-        // ---- online softmax on rows g (values c0, c1 of each n-tile) ----
-        float s[4];
+        // ---- online softmax on row g: values c0, c1 of each n-tile ----
+        float sv[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < 8; ++e) {
           const int tok = p0 + (e >> 1) * 8 + 2 * tq + (e & 1);
-          s[e] = tok < ntok ? sacc[e >> 1][e & 1] * sl2 : -INFINITY;
+          sv[e] = tok < ntok ? sacc[e >> 1][e & 1] * sl2 : -INFINITY;
         }
-        float mx = fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3]));
+        float mx = sv[0];
+#pragma unroll
+        for (int e = 1; e < 8; ++e) mx = fmaxf(mx, sv[e]);
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         const float mn = fmaxf(m, mx);
         const float corr = exp2f(m - mn);
         m = mn;
-        float pr[4];
+        float pr[8];
+        float ps = 0.f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) pr[e] = exp2f(s[e] - mn);
-        l = l * corr + (pr[0] + pr[1]) + (pr[2] + pr[3]);
+        for (int e = 0; e < 8; ++e) {
+          pr[e] = exp2f(sv[e] - mn);
+          ps += pr[e];
+        }
+        l = l * corr + ps;
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
           o[n][0] *= corr;
           o[n][1] *= corr;
         }
+        // A operands of P.V: k-tile h2 covers tokens 16*h2 .. 16*h2+15
         const uint32_t pa0 = MmaType<T>::pack(pr[0], pr[1]);  // P[g][2tq, 2tq+1]
-        const uint32_t pa2 = MmaType<T>::pack(pr[2], pr[3]);  // P[g][8+2tq, 8+2tq+1]
-        // ---- O += P V for tokens p0 .. p0+15 ----
+        const uint32_t pa2 = MmaType<T>::pack(pr[2], pr[3]);  // P[g][8+2tq, +1]
+        const uint32_t pb0 = MmaType<T>::pack(pr[4], pr[5]);  // P[g][16+2tq, +1]
+        const uint32_t pb2 = MmaType<T>::pack(pr[6], pr[7]);  // P[g][24+2tq, +1]
+        // ---- O += P V ----
 #pragma unroll
         for (int n = 0; n < NT; n += 2) {
+          const uint32_t off = (uint32_t)((n >> 3) * hb_bytes);
           // matrices: (tok 0-7, d n*8..), (tok 8-15, d n*8..), (tok 0-7, d n*8+8..), (tok 8-15, d n*8+8..)
-          uint32_t b[4];
-          ldsm_x4_trans(vrow + (uint32_t)((n >> 3) * hb_bytes) + (((((uint32_t)n & 7u) + vc) ^ vx) << 4), b);
-          mma16816<T>(o[n], pa0, pa2, b[0], b[1]);
-          mma16816<T>(o[n + 1], pa0, pa2, b[2], b[3]);
+          uint32_t b0[4], b1[4];
+          ldsm_x4_trans(vrow[0] + off + (((((uint32_t)n & 7u) + vc) ^ vx[0]) << 4), b0);
+          ldsm_x4_trans(vrow[1] + off + (((((uint32_t)n & 7u) + vc) ^ vx[1]) << 4), b1);
+          mma16816<T>(o[n], pa0, pa2, b0[0], b0[1]);
+          mma16816<T>(o[n + 1], pa0, pa2, b0[2], b0[3]);
+          mma16816<T>(o[n], pb0, pb2, b1[0], b1[1]);
+          mma16816<T>(o[n + 1], pb0, pb2, b1[2], b1[3]);
         }
       }
       if (ntok < TT) fence_proxy_async_smem();  // order the zero-fill before the slot's next bulk copy
@@ -276,13 +308,17 @@ int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
   const int bs = pool.block_size;
   // Stages of >= 32 tokens: fixed per-stage costs (barrier round trips, copy
   // issue) halve against 16-token stages.
-  const int sb = bs >= 32 ? 1 : 32 / bs;
+  const char* env_st = getenv("CLOVE_TUNE_STAGE_TOKENS");
+  const int st_tok = env_st ? atoi(env_st) : 32;
+  const int sb = bs >= st_tok ? 1 : min(4, st_tok / bs);  // stages hold a multiple of 32 tokens
   a.stage_blocks = sb;
+  const char* env_ring = getenv("CLOVE_TUNE_RING_KB");
+  const int ring_target = env_ring ? atoi(env_ring) * 1024 : kMmaRingTarget;
   const int scratch = kMmaNCW * 8 * (D + 2) * 4;
   const int qb = 8 * D * (int)sizeof(T);
   SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb);
   int ncw = kMmaNCW;
-  int nstage = (kMmaRingTarget / sp.stage_bytes) / ncw * ncw;
+  int nstage = (ring_target / sp.stage_bytes) / ncw * ncw;
   if (nstage < ncw) nstage = ncw;
   if (nstage > 4 * ncw) nstage = 4 * ncw;
   sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);

@@ -106,3 +106,35 @@ def test_pool_create_owns_memory():
     assert info.owns_memory == 1 and info.plane_bytes == 128 * 16 * 8 * 64 * 2
     assert info.v_cache - info.k_cache == info.plane_bytes
     _lib.check(L.clove_cuda_pool_destroy(h))
+
+
+@pytest.mark.parametrize("variant,group", [("mma", 4), ("mma", 2), ("simt", 3), ("simt", 1)])
+def test_workspace_writes_stay_in_bounds(variant, group):
+    # Multi-chunk sequences at the end of the batch write split-K partials at
+    # the top of the workspace: a guard region right after the reported size
+    # must come back untouched.
+    from clove_b200 import set_decode_variant
+    from clove_b200.workload import Spec, fill_values, make_layout
+    from clove_b200 import KVPool
+    spec = Spec("t", 64, 2 * group, 2, 128, 16, 0, torch.bfloat16, "uniform", 600, 3000, "permutation", seed=17)
+    lay = make_layout(spec)
+    dev = torch.device("cuda", 0)
+    pool = KVPool(lay.num_blocks, 16, 2, 128, torch.bfloat16, 0)
+    q, kn, vn, _ = fill_values(lay, dev, pool.storage)
+    need = pool.workspace_bytes(lay.batch, spec.num_q_heads, lay.max_ctx)
+    buf = torch.full((need + 65536,), 0xAB, dtype=torch.uint8, device=dev)
+    out = torch.empty((lay.batch, spec.num_q_heads, 128), device=dev)
+    bt = torch.from_numpy(lay.block_tables).to(dev)
+    cl = torch.from_numpy(lay.context_lens).to(dev)
+    set_decode_variant(variant)
+    try:
+        rc = _lib.lib().clove_cuda_paged_append_decode(
+            pool.handle, q.data_ptr(), kn.data_ptr(), vn.data_ptr(), spec.num_q_heads, bt.data_ptr(),
+            bt.shape[1], cl.data_ptr(), lay.batch, 0.0884, lay.max_ctx, out.data_ptr(), buf.data_ptr(), need,
+            None)
+        _lib.check(rc)
+        torch.cuda.synchronize()
+    finally:
+        set_decode_variant("auto")
+    assert (buf[need:] == 0xAB).all(), "decode wrote past the workspace size it reported"
+    assert torch.isfinite(out).all()
