@@ -125,6 +125,9 @@ __device__ __forceinline__ void init_barriers(const SmemPtrs& p, int nstage) {
     fence_barrier_init();
   }
   __syncthreads();
+  // Launched as a programmatic dependent of the plan kernel: from here on the
+  // kernel reads the plan's outputs, so wait for that grid to finish.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // K tiles of a stage are at [0, sb) * tile_stride, V tiles at

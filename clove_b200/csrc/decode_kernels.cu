@@ -30,6 +30,7 @@
 // Semantics follow the reference's documented op: softmax(q.K^T * scale).V
 // (src/nn/attention.rs:52-69), scale 1/sqrt(head_dim) supplied by the caller
 // (src/lazy.rs:5267), block-table gather of src/lazy.rs:5259-5270.
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -87,6 +88,13 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
   __shared__ long long s_blocks;
   __shared__ int s_full;
   const int tid = threadIdx.x, lane = tid & 31;
+  // Let the decode kernel launch now: it sets up its barriers and then waits
+  // (griddepcontrol.wait) for this grid's results.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // Context lengths of this thread's first sequence stay in registers; only
+  // batches beyond kPlanThreads sequences re-read the rest.
+  const int b0 = tid;
+  const int L0 = b0 < p.batch ? clamp_ctx(p.context_lens, b0, p.max_ctx, p.append) : 0;
   if (tid == 0) {
     s_blocks = 0;
     s_full = 0;
@@ -95,14 +103,12 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
   }
   for (int i = tid; i < kPlanBins; i += kPlanThreads) hist[i] = 0;
   __syncthreads();
+  auto len_of = [&](int b) { return b == b0 ? L0 : clamp_ctx(p.context_lens, b, p.max_ctx, p.append); };
   // Chunk size from the actual work: total (block, KV head) pairs spread
   // over ~target_units work items, never below min_chunk_blocks.
   {
     long long mine = 0;
-    for (int b = tid; b < p.batch; b += kPlanThreads) {
-      const int L = clamp_ctx(p.context_lens, b, p.max_ctx, p.append);
-      mine += (L + p.block_size - 1) / p.block_size;
-    }
+    for (int b = tid; b < p.batch; b += kPlanThreads) mine += (len_of(b) + p.block_size - 1) / p.block_size;
     for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
     if (lane == 0 && mine) atomicAdd(reinterpret_cast<unsigned long long*>(&s_blocks), (unsigned long long)mine);
   }
@@ -116,8 +122,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
     const int b = base + tid;
     int nfull = 0;
     if (b < p.batch) {
-      const int raw = p.context_lens[b];
-      const int L = clamp_ctx(p.context_lens, b, p.max_ctx, p.append);
+      const int raw = __ldg(p.context_lens + b);
+      const int L = len_of(b);
       if (raw != L - p.append) atomicOr(p.err, CLOVE_FLAG_CTX_RANGE);
       const int nbl = (L + p.block_size - 1) / p.block_size;
       nfull = nbl / cb;
@@ -137,19 +143,22 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
     if (tid == 0) s_full += tot;
     __syncthreads();
   }
-  // partial chunks: bases per size bin, largest bin first
-  if (tid == 0) {
-    int acc = s_full;
-    for (int bin = kPlanBins - 1; bin >= 0; --bin) {
-      binbase[bin] = acc;
-      acc += hist[bin];
+  // partial chunks: bases per size bin, largest bin first (parallel scan over
+  // the bins in descending order)
+  {
+    const int bin = kPlanBins - 1 - tid;
+    const int cnt = tid < kPlanBins ? hist[bin] : 0;
+    int tot;
+    const int excl = block_excl_scan(cnt, warp_tot, &tot);
+    if (tid < kPlanBins) {
+      binbase[bin] = s_full + excl;
       hist[bin] = 0;  // reused as the per-bin cursor
     }
-    *p.n_items = acc;
+    if (tid == 0) *p.n_items = s_full + tot;
   }
   __syncthreads();
   for (int b = tid; b < p.batch; b += kPlanThreads) {
-    const int L = clamp_ctx(p.context_lens, b, p.max_ctx, p.append);
+    const int L = len_of(b);
     const int nbl = (L + p.block_size - 1) / p.block_size;
     const int nfull = nbl / cb;
     const int rem = nbl - nfull * cb;
@@ -434,8 +443,7 @@ static int run_simt(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) 
   long long grid = (long long)pool.num_sms * occ;
   if (grid > units_max) grid = units_max;
   if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, (kNCW + 1) * 32, sp.total, stream>>>(pool.tm_k, pool.tm_v, a);
-  e = cudaGetLastError();
+  e = launch_dependent(kern, (unsigned)grid, (kNCW + 1) * 32, sp.total, stream, pool.tm_k, pool.tm_v, a);
   if (e != cudaSuccess) {
     set_last_error("paged_decode launch: %s", cudaGetErrorString(e));
     return CLOVE_ERR_CUDA;
@@ -500,7 +508,7 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   p.row_floats = call.num_q_heads * pool.head_dim;
   p.block_size = pool.block_size;
   p.min_chunk_blocks = L.chunk_blocks;
-  p.target_units = (long long)pool.num_sms * 8;  // ~4 units per resident CTA at 2 CTAs/SM
+  p.target_units = (long long)pool.num_sms * 4;  // ~2 units per resident CTA (measured best on C2-C5)
   p.chunk_blocks = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 1;
   p.unit_counter = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 2;
   p.max_ctx = call.max_ctx;

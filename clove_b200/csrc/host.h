@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "../../include/clove_cuda.h"
+#include "common.cuh"
 
 // The pool handle behind clove_pool_t.
 struct clove_pool {
@@ -70,6 +71,25 @@ cudaError_t launch_gather_kv(const void* k_cache, const void* v_cache, const int
                              int bt_stride, const int32_t* context_lens, int batch, int max_ctx,
                              int block_size, int num_blocks, int row_bytes, void* k_out, void* v_out,
                              int32_t* flags, cudaStream_t stream);
+
+// Launch a decode kernel as a programmatic dependent of the previous kernel
+// on the stream (the plan): it may start early and must execute
+// griddepcontrol.wait before reading the plan's outputs.
+template <typename Kern>
+cudaError_t launch_dependent(Kern kern, unsigned grid, unsigned threads, size_t smem, cudaStream_t stream,
+                             const CUtensorMap& tk, const CUtensorMap& tv, const DecodeArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tk, tv, a);
+}
 
 // error text / launch accounting (capi.cu)
 void set_last_error(const char* fmt, ...);

@@ -349,8 +349,7 @@ int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
   long long grid = (long long)pool.num_sms * occ;
   if (grid > units_max) grid = units_max;
   if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, (kMmaNCW + 1) * 32, smem, stream>>>(pool.tm_k_sw, pool.tm_v_sw, a);
-  e = cudaGetLastError();
+  e = launch_dependent(kern, (unsigned)grid, (kMmaNCW + 1) * 32, smem, stream, pool.tm_k_sw, pool.tm_v_sw, a);
   if (e != cudaSuccess) {
     set_last_error("paged_decode (mma) launch: %s", cudaGetErrorString(e));
     return CLOVE_ERR_CUDA;
