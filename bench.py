@@ -27,6 +27,12 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "paged-attn decode tokens/s"
 
+# DRAM bytes (read + write) per decode launch on rank 0's default workload,
+# from the ncu captures summarised in profiles/ (paged_decode_simt_c2.md,
+# paged_decode_mma_c3_c5.md).  Reported as roofline.traffic next to the
+# algorithmic bytes; None where no full-size capture exists.
+TRAFFIC_MEASURED = {"c2": 4338.4e6, "c3": 694.1e6}
+
 
 def _peaks() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
@@ -174,17 +180,34 @@ def run_ours(args) -> None:
     from clove_b200 import KVPool, launch_count
     from clove_b200.workload import CONFIGS, fill_values, make_layout
 
+    from dataclasses import replace
+
+    from clove_b200.distributed import head_sharded_append_decode
+
     ws, rank, local = _dist()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     spec = CONFIGS[args.config]
-    # weak scaling: one full workload per rank (--batch shrinks it for profiling)
     if args.batch is not None:
-        from dataclasses import replace
-        spec = replace(spec, num_blocks=0)  # pool sized to the blocks used
-    lay = make_layout(spec, seed=spec.seed + rank, batch=args.batch)
-    pool = KVPool(lay.num_blocks, spec.block_size, spec.num_kv_heads, spec.head_dim, spec.dtype, dev)
-    q, kn, vn, _ = fill_values(lay, dev, pool.storage)
+        spec = replace(spec, num_blocks=0)  # pool sized to the blocks used (profiling)
+    # c4 on N > 1 GPUs: KV heads split across ranks + one all-gather of the
+    # outputs (strong scaling: the same 8 sequences).  Every other run: one full
+    # workload per rank, sequences independent (weak scaling).
+    head_split = spec.name == "c4" and ws > 1
+    if head_split:
+        lay = make_layout(spec, seed=spec.seed, batch=args.batch)  # same tables on every rank
+        lspec = replace(spec, num_kv_heads=spec.num_kv_heads // ws, num_q_heads=spec.num_q_heads // ws,
+                        seed=spec.seed + rank)
+        llay = replace(lay, spec=lspec, seed=lspec.seed)
+        pool = KVPool(lay.num_blocks, spec.block_size, lspec.num_kv_heads, spec.head_dim, spec.dtype, dev)
+        _, kn, vn, _ = fill_values(llay, dev, pool.storage)
+        gq = torch.Generator(device=dev)
+        gq.manual_seed(spec.seed)
+        q = torch.randn((lay.batch, spec.num_q_heads, spec.head_dim), generator=gq, device=dev).to(spec.dtype)
+    else:
+        lay = make_layout(spec, seed=spec.seed + rank, batch=args.batch)
+        pool = KVPool(lay.num_blocks, spec.block_size, spec.num_kv_heads, spec.head_dim, spec.dtype, dev)
+        q, kn, vn, _ = fill_values(lay, dev, pool.storage)
     bt = torch.from_numpy(lay.block_tables).to(dev)
     cl = torch.from_numpy(lay.context_lens).to(dev)
     out = torch.empty((lay.batch, spec.num_q_heads, spec.head_dim), dtype=torch.float32, device=dev)
@@ -192,7 +215,9 @@ def run_ours(args) -> None:
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        pool.append_decode(q, kn, vn, bt, cl, max_ctx=max_ctx, out=out, stream=stream)
+        if head_split:
+            return head_sharded_append_decode(pool, q, kn, vn, bt, cl, ws, rank, max_ctx)
+        return pool.append_decode(q, kn, vn, bt, cl, max_ctx=max_ctx, out=out, stream=stream)
 
     def barrier():
         if ws > 1:
@@ -235,8 +260,11 @@ def run_ours(args) -> None:
     def e2e_step():
         for d, h in ((dq, hq), (dk, hk), (dv, hv), (dbt, hbt), (dcl, hcl)):
             d.copy_(h, non_blocking=True)
-        pool.append_decode(dq, dk, dv, dbt, dcl, max_ctx=max_ctx, out=out, stream=stream)
-        hout.copy_(out, non_blocking=True)
+        if head_split:
+            res = head_sharded_append_decode(pool, dq, dk, dv, dbt, dcl, ws, rank, max_ctx)
+        else:
+            res = pool.append_decode(dq, dk, dv, dbt, dcl, max_ctx=max_ctx, out=out, stream=stream)
+        hout.copy_(res, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -254,8 +282,8 @@ def run_ours(args) -> None:
 
     if rank != 0:
         return
-    tokens = lay.batch * ws
-    kv_bytes = lay.kv_bytes()  # per rank per step
+    tokens = lay.batch * (1 if head_split else ws)
+    kv_bytes = lay.kv_bytes() // (ws if head_split else 1)  # per rank per step
     achieved = kv_bytes / (ms * 1e-3) / 1e9
     peak, peak_kind = _peaks()
     cb = None
@@ -265,15 +293,20 @@ def run_ours(args) -> None:
     line = {
         "metric": METRIC, "value": tokens / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": _dtype_name(spec.dtype), "data": "synthetic",
+        "scaling": "strong" if head_split else "weak", "vs_baseline": None, "dtype": _dtype_name(spec.dtype),
+        "data": "synthetic",
         "config": {"workload": spec.name, "description": spec.description, "batch_per_gpu": lay.batch,
                    "global_batch": tokens, "num_q_heads": spec.num_q_heads, "num_kv_heads": spec.num_kv_heads,
                    "head_dim": spec.head_dim, "block_size": spec.block_size, "num_blocks": lay.num_blocks,
                    "kv_bytes_per_gpu_step": kv_bytes, "l2": "inputs larger than L2 (no flush)",
-                   "parallelism": f"dp{ws} (independent sequences per GPU)"},
+                   "parallelism": (f"kv-heads/{ws} + all-gather" if head_split
+                                   else f"dp{ws} (independent sequences per GPU)")},
         "hbm_gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": args.traffic,
+                     "frac": achieved / peak,
+                     "traffic": (args.traffic if args.traffic is not None
+                                 else None if (args.batch is not None or head_split)
+                                 else TRAFFIC_MEASURED.get(spec.name)),
                      "note": f"KV bytes per step / whole step time (plan + decode kernels), peak {peak_kind}"},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
