@@ -257,23 +257,50 @@ def run_ours(args) -> None:
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hbt, hcl))
     d2h = hout.numel() * 4
 
-    def e2e_step():
-        for d, h in ((dq, hq), (dk, hk), (dv, hv), (dbt, hbt), (dcl, hcl)):
-            d.copy_(h, non_blocking=True)
-        if head_split:
+    if head_split:
+        def e2e_step():
+            for d, h in ((dq, hq), (dk, hk), (dv, hv), (dbt, hbt), (dcl, hcl)):
+                d.copy_(h, non_blocking=True)
             res = head_sharded_append_decode(pool, dq, dk, dv, dbt, dcl, ws, rank, max_ctx)
-        else:
-            res = pool.append_decode(dq, dk, dv, dbt, dcl, max_ctx=max_ctx, out=out, stream=stream)
-        hout.copy_(res, non_blocking=True)
+            hout.copy_(res, non_blocking=True)
+    else:
+        # Through the reference-facing FFI (include/clove_ffi.h): tensors made
+        # from host buffers, clove_paged_attention, result copied back to host.
+        import ctypes as C
+
+        from clove_b200 import _lib
+        L = _lib.lib()
+        code = {torch.float32: 0, torch.bfloat16: 160, torch.float16: 16}[spec.dtype]
+
+        def mk(t, dt):
+            shp = (C.c_int64 * t.dim())(*t.shape)
+            h = L.clove_tensor_create_nd(t.data_ptr(), shp, t.dim(), dt, local)
+            if not h:
+                raise RuntimeError(_lib.last_error())
+            return h
+
+        kv_shape = (C.c_int64 * 5)(*pool.storage.shape)
+        kv_h = L.clove_tensor_from_device(pool.storage.data_ptr(), kv_shape, 5, code, local)
+        hq2, hk2, hv2 = hq.view(lay.batch, -1), hk.view(lay.batch, -1), hv.view(lay.batch, -1)
+
+        def e2e_step():
+            hs = [mk(hq2, code), mk(hk2, code), mk(hv2, code), mk(hbt, 32), mk(hcl, 32)]
+            o = L.clove_paged_attention(hs[0], hs[1], hs[2], kv_h, hs[3], hs[4])
+            if not o:
+                raise RuntimeError(_lib.last_error())
+            L.clove_tensor_data(o, hout.data_ptr())
+            for h in hs + [o]:
+                L.clove_tensor_free(h)
 
     for _ in range(3):
         e2e_step()
     barrier()
     torch.cuda.synchronize()
-    ev0.record(stream)
+    e2e_stream = stream if head_split else torch.cuda.default_stream(dev)  # the FFI runs on the legacy stream
+    ev0.record(e2e_stream)
     for _ in range(args.steps):
         e2e_step()
-    ev1.record(stream)
+    ev1.record(e2e_stream)
     torch.cuda.synchronize()
     te = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev, dtype=torch.float64)
     if ws > 1:

@@ -61,6 +61,22 @@ SIGNATURES = {
 }
 
 
+DTYPE_I32 = 32
+_i64p = C.POINTER(C.c_int64)
+
+# include/clove_ffi.h: the reference-facing tensor-handle FFI.
+FFI_SIGNATURES = {
+    "clove_tensor_create": (_vp, [C.POINTER(C.c_float), _sz, _sz]),
+    "clove_tensor_create_nd": (_vp, [_vp, _i64p, _i, _i, _i]),
+    "clove_tensor_from_device": (_vp, [_vp, _i64p, _i, _i, _i]),
+    "clove_tensor_free": (None, [_vp]),
+    "clove_tensor_data": (None, [_vp, _vp]),
+    "clove_tensor_shape": (_i, [_vp, _i64p]),
+    "clove_paged_attention": (_vp, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "clove_tensor_cache_bytes": (_sz, [_i]),
+}
+
+
 def load(path: Path | str = LIB_PATH) -> C.CDLL:
     path = Path(path)
     if not path.exists():
@@ -68,7 +84,7 @@ def load(path: Path | str = LIB_PATH) -> C.CDLL:
             f"{path} is missing: build it with `python -m clove_b200.build` "
             "(the CUDA extension is required; there is no fallback)")
     lib = C.CDLL(str(path))
-    for name, (res, args) in SIGNATURES.items():
+    for name, (res, args) in {**SIGNATURES, **FFI_SIGNATURES}.items():
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args

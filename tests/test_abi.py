@@ -39,6 +39,20 @@ def test_bindings_cover_header():
     assert declared == set(_lib.SIGNATURES), declared ^ set(_lib.SIGNATURES)
 
 
+def test_ffi_bindings_cover_header():
+    from clove_b200 import _lib
+    declared = _declared(ROOT / "include" / "clove_ffi.h")
+    assert declared == set(_lib.FFI_SIGNATURES), declared ^ set(_lib.FFI_SIGNATURES)
+
+
+def test_ffi_null_handles(lib):
+    assert lib.clove_tensor_create(None, 2, 2) is None
+    assert lib.clove_paged_attention(None, None, None, None, None, None) is None
+    lib.clove_tensor_free(None)
+    lib.clove_tensor_data(None, None)
+    assert lib.clove_tensor_shape(None, None) == -1
+
+
 def test_last_error_and_variant(lib):
     assert lib.clove_cuda_set_decode_variant(7) == -1
     buf = C.create_string_buffer(256)
