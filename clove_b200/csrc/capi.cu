@@ -56,17 +56,31 @@ static int encode_plane_map(CUtensorMap* map, void* base, const clove_pool& p, b
   CUtensorMapDataType dt = p.dtype == CLOVE_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                            : p.dtype == CLOVE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  // dims innermost first: head_dim, kv head, token slot (block*block_size+off)
-  cuuint64_t dims[3] = {(cuuint64_t)p.head_dim, (cuuint64_t)p.num_kv_heads,
-                        (cuuint64_t)p.num_blocks * (cuuint64_t)p.block_size};
-  cuuint64_t strides[2] = {(cuuint64_t)p.head_dim * p.elem_bytes,
-                           (cuuint64_t)p.num_kv_heads * p.head_dim * p.elem_bytes};
-  cuuint32_t box[3] = {(cuuint32_t)(swizzled ? 64 : p.head_dim), 1u, (cuuint32_t)p.block_size};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, dt, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzled ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (!swizzled) {
+    // 3-D, dims innermost first: head_dim, kv head, token slot (block*block_size+off)
+    cuuint64_t dims[3] = {(cuuint64_t)p.head_dim, (cuuint64_t)p.num_kv_heads,
+                          (cuuint64_t)p.num_blocks * (cuuint64_t)p.block_size};
+    cuuint64_t strides[2] = {(cuuint64_t)p.head_dim * p.elem_bytes,
+                             (cuuint64_t)p.num_kv_heads * p.head_dim * p.elem_bytes};
+    cuuint32_t box[3] = {(cuuint32_t)p.head_dim, 1u, (cuuint32_t)p.block_size};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = fn(map, dt, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    // 4-D for the 128-byte swizzle: head_dim split into 64-element (128-byte)
+    // halves (d_lo, d_hi), kv head, token slot.  One box = a whole
+    // [block_size, head_dim] tile, laid out as 128-byte rows (token, d_hi).
+    const int nh = p.head_dim / 64;
+    cuuint64_t dims[4] = {64, (cuuint64_t)nh, (cuuint64_t)p.num_kv_heads,
+                          (cuuint64_t)p.num_blocks * (cuuint64_t)p.block_size};
+    cuuint64_t strides[3] = {128, (cuuint64_t)p.head_dim * p.elem_bytes,
+                             (cuuint64_t)p.num_kv_heads * p.head_dim * p.elem_bytes};
+    cuuint32_t box[4] = {64, (cuuint32_t)nh, 1u, (cuuint32_t)p.block_size};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    r = fn(map, dt, 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) {
     set_last_error("cuTensorMapEncodeTiled failed (%d) for head_dim %d block_size %d", (int)r, p.head_dim,
                    p.block_size);

@@ -154,6 +154,16 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+// 4-D tiled bulk tensor load (the swizzled K/V maps); c0 = 0 always.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Make this thread's generic-proxy global writes visible to later async-proxy
 // (TMA) reads.
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -175,6 +185,12 @@ __device__ __forceinline__ int named_bar_or(int id, int nthreads, int pred) {
       : "r"(pred), "r"(id), "r"(nthreads)
       : "memory");
   return r;
+}
+
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -217,6 +233,8 @@ struct DecodeArgs {
   int nstage;                // pipeline depth (a multiple of ncw)
   int ncw;                   // consumer warps that take stages (<= the kernel's NCW)
   int stage_blocks;          // blocks per pipeline stage (1..4)
+  int exp_skip;              // EXPERIMENT: consumers skip the math
+  unsigned long long* exp_times;  // EXPERIMENT: per-CTA timestamps (null normally)
   float qscale;              // scale * log2(e)
 };
 

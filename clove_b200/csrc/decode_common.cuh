@@ -110,7 +110,7 @@ __device__ __forceinline__ SmemPtrs smem_ptrs(unsigned char* base, const SmemPla
 }
 
 // Barrier initialisation (thread 0), then a CTA barrier.
-__device__ __forceinline__ void init_barriers(const SmemPtrs& p, int nstage) {
+__device__ __forceinline__ void init_barriers(const SmemPtrs& p, int nstage, unsigned long long* a_exp_times = nullptr) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < nstage; ++s) {
       mbar_init(&p.full[s], 1);
@@ -125,9 +125,14 @@ __device__ __forceinline__ void init_barriers(const SmemPtrs& p, int nstage) {
     fence_barrier_init();
   }
   __syncthreads();
+  unsigned long long t0 = gtimer();
   // Launched as a programmatic dependent of the plan kernel: from here on the
   // kernel reads the plan's outputs, so wait for that grid to finish.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (a_exp_times && threadIdx.x == 0) {
+    a_exp_times[blockIdx.x * 4 + 0] = t0;
+    a_exp_times[blockIdx.x * 4 + 1] = gtimer();
+  }
 }
 
 // K tiles of a stage are at [0, sb) * tile_stride, V tiles at
@@ -172,9 +177,9 @@ __device__ __forceinline__ void append_row(const DecodeArgs& a, const Unit& x, i
 // 0 issues copies.  On a stuck wait it raises the abort flag and drains its
 // own in-flight copies (bounded) before returning.
 //
-// NBOX: boxes per tile.  1 = one [block_size, head_dim] box (dense rows);
-// D/64 = head_dim split into 64-element (128-byte) boxes written with the
-// 128-byte swizzle, sub-tile hb at tile offset hb * block_size * 128.
+// NBOX: 1 = one 3-D [block_size, head_dim] box per tile (dense rows); 2 =
+// one 4-D box per tile written with the 128-byte swizzle as
+// 128-byte rows (token, 64-dim half).
 template <typename T, int D, int NBOX>
 __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUtensorMap* tm_v, const SmemPtrs& sm,
                         const SmemPlan& sp, int sb, int n_units) {
@@ -265,13 +270,12 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             if (i < nb) {
-#pragma unroll
-              for (int hb = 0; hb < NBOX; ++hb) {
-                const int off = hb * (D / NBOX) * (int)sizeof(T) * bs;
-                tma_load_3d(st + i * sp.tile_stride + off, tm_k, &sm.full[slot], hb * (D / NBOX), x.h, phys[i] * bs,
-                            pol);
-                tma_load_3d(st + (sb + i) * sp.tile_stride + off, tm_v, &sm.full[slot], hb * (D / NBOX), x.h,
-                            phys[i] * bs, pol);
+              if constexpr (NBOX == 1) {
+                tma_load_3d(st + i * sp.tile_stride, tm_k, &sm.full[slot], 0, x.h, phys[i] * bs, pol);
+                tma_load_3d(st + (sb + i) * sp.tile_stride, tm_v, &sm.full[slot], 0, x.h, phys[i] * bs, pol);
+              } else {
+                tma_load_4d(st + i * sp.tile_stride, tm_k, &sm.full[slot], 0, 0, x.h, phys[i] * bs, pol);
+                tma_load_4d(st + (sb + i) * sp.tile_stride, tm_v, &sm.full[slot], 0, 0, x.h, phys[i] * bs, pol);
               }
             }
           }

@@ -548,6 +548,8 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   a.group = call.num_q_heads / pool.num_kv_heads;
   a.append = append;
   a.nstage = 2;
+  a.exp_skip = 0;
+  a.exp_times = nullptr;
   a.ncw = 1;
   a.qscale = call.scale * kLog2e;
 

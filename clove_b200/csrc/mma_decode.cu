@@ -84,10 +84,10 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 // Byte offset, inside a stage's K (or V) region, of 16-byte chunk `ch`
 // (head_dim / 8 chunks per token) of token `tok` (0 .. sb*block_size-1).
-__device__ __forceinline__ uint32_t swz_off(int tok, int ch, int bs, int tile_stride) {
+__device__ __forceinline__ uint32_t swz_off(int tok, int ch, int bs, int tile_stride, int nh) {
   const int blk = tok / bs, r = tok - blk * bs;
-  const int hb = ch >> 3, c = ch & 7;
-  return (uint32_t)(blk * tile_stride + (hb * bs + r) * 128 + ((c ^ (r & 7)) << 4));
+  const int row = r * nh + (ch >> 3);  // 128-byte row (token, 64-dim half) within the tile
+  return (uint32_t)(blk * tile_stride + row * 128 + (((ch & 7) ^ (row & 7)) << 4));
 }
 
 // NCW consumer warps; D = 64 or 128.  Each consumer warp owns whole stages;
@@ -114,11 +114,11 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
                                 G * D * (int)sizeof(T));
   const SmemPtrs sm = smem_ptrs(smem, sp, a.nstage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  init_barriers(sm, a.nstage);
+  init_barriers(sm, a.nstage, a.exp_times);
   const int n_units = *a.n_items * a.num_kv_heads;
 
   if (warp == 0) {
-    produce<T, D, D / 64>(a, &tm_k, &tm_v, sm, sp, sb, n_units);
+    produce<T, D, 2>(a, &tm_k, &tm_v, sm, sp, sb, n_units);
     return;
   }
 
@@ -170,6 +170,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         aborted = true;
         break;
       }
+      if (a.exp_times && gs == 0 && lane == 0) a.exp_times[blockIdx.x * 4 + 2] = gtimer();
       unsigned char* kst = sm.ring + (size_t)slot * sp.stage_bytes;
       unsigned char* vst = kst + sb * sp.tile_stride;
       const int ntok = min(TT, x.L - (x.blk0 + j * sb) * bs);
@@ -178,26 +179,28 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         // zero there but 0 * NaN is NaN inside the MMA, so clear those V rows.
         for (int i = lane; i < (TT - ntok) * (D / 8); i += 32) {
           const int tok = ntok + i / (D / 8), ch = i % (D / 8);
-          *reinterpret_cast<uint4*>(vst + swz_off(tok, ch, bs, sp.tile_stride)) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(vst + swz_off(tok, ch, bs, sp.tile_stride, D / 64)) = make_uint4(0, 0, 0, 0);
         }
         __syncwarp();
       }
       const uint32_t kbase = smem_u32(kst), vbase = smem_u32(vst);
-      const int hb_bytes = bs * 128;  // one 64-dim sub-tile
-      for (int p0 = 0; p0 < ntok; p0 += 32) {
+      constexpr int NH = D / 64;  // 128-byte rows per token
+      for (int p0 = 0; p0 < (a.exp_skip ? 0 : ntok); p0 += 32) {
         // 32 tokens per pass, as two 16-token halves h = 0, 1.  Per-pass
         // ldmatrix row addresses: chunk ch of token tok lives at
-        // row_off(tok) + (ch >> 3) * hb_bytes + (((ch & 7) ^ (tok_row & 7)) << 4).
-        uint32_t krow[2], kx[2], vrow[2], vx[2];
+        // tile_off(tok) + row * 128 + (((ch & 7) ^ (row & 7)) << 4), with
+        // row = token_in_block * NH + (ch >> 3) (the layout of the 4-D box).
+        uint32_t krow[2], vrow[2];
+        int kr[2], vr[2];
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
           const int tk_k = p0 + 16 * h2 + (mi >> 1) * 8 + mr, tk_v = p0 + 16 * h2 + (mi & 1) * 8 + mr;
           const int bk = tk_k / bs, rk = tk_k - bk * bs;
           const int bv = tk_v / bs, rv = tk_v - bv * bs;
-          krow[h2] = kbase + (uint32_t)(bk * sp.tile_stride + rk * 128);
-          kx[h2] = (uint32_t)(rk & 7);
-          vrow[h2] = vbase + (uint32_t)(bv * sp.tile_stride + rv * 128);
-          vx[h2] = (uint32_t)(rv & 7);
+          kr[h2] = rk * NH;
+          vr[h2] = rv * NH;
+          krow[h2] = kbase + (uint32_t)(bk * sp.tile_stride + kr[h2] * 128);
+          vrow[h2] = vbase + (uint32_t)(bv * sp.tile_stride + vr[h2] * 128);
         }
         const uint32_t kc = (uint32_t)(mi & 1), vc = (uint32_t)(mi >> 1);
         // ---- S = Q K^T: 4 n-tiles of 8 tokens, 4 independent MMA chains ----
@@ -206,11 +209,12 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         for (int j = 0; j < 4; ++j) sacc[j][0] = sacc[j][1] = 0.f;
 #pragma unroll
         for (int k = 0; k < KS; ++k) {
-          const uint32_t off = (uint32_t)((k >> 2) * hb_bytes);
+          const int hb = k >> 2;  // which 64-dim half
+          const uint32_t off = (uint32_t)(hb * 128);
           // matrices: (tok 0-7, d 0-7), (tok 0-7, d 8-15), (tok 8-15, d 0-7), (tok 8-15, d 8-15)
           uint32_t b0[4], b1[4];
-          ldsm_x4(krow[0] + off + (((((uint32_t)(2 * k) & 7u) + kc) ^ kx[0]) << 4), b0);
-          ldsm_x4(krow[1] + off + (((((uint32_t)(2 * k) & 7u) + kc) ^ kx[1]) << 4), b1);
+          ldsm_x4(krow[0] + off + (((((uint32_t)(2 * k) & 7u) + kc) ^ (uint32_t)((kr[0] + hb) & 7)) << 4), b0);
+          ldsm_x4(krow[1] + off + (((((uint32_t)(2 * k) & 7u) + kc) ^ (uint32_t)((kr[1] + hb) & 7)) << 4), b1);
           mma16816<T>(sacc[0], qa[k][0], qa[k][1], b0[0], b0[1]);
           mma16816<T>(sacc[1], qa[k][0], qa[k][1], b0[2], b0[3]);
           mma16816<T>(sacc[2], qa[k][0], qa[k][1], b1[0], b1[1]);
@@ -252,11 +256,12 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         // ---- O += P V ----
 #pragma unroll
         for (int n = 0; n < NT; n += 2) {
-          const uint32_t off = (uint32_t)((n >> 3) * hb_bytes);
+          const int hb = n >> 3;
+          const uint32_t off = (uint32_t)(hb * 128);
           // matrices: (tok 0-7, d n*8..), (tok 8-15, d n*8..), (tok 0-7, d n*8+8..), (tok 8-15, d n*8+8..)
           uint32_t b0[4], b1[4];
-          ldsm_x4_trans(vrow[0] + off + (((((uint32_t)n & 7u) + vc) ^ vx[0]) << 4), b0);
-          ldsm_x4_trans(vrow[1] + off + (((((uint32_t)n & 7u) + vc) ^ vx[1]) << 4), b1);
+          ldsm_x4_trans(vrow[0] + off + (((((uint32_t)n & 7u) + vc) ^ (uint32_t)((vr[0] + hb) & 7)) << 4), b0);
+          ldsm_x4_trans(vrow[1] + off + (((((uint32_t)n & 7u) + vc) ^ (uint32_t)((vr[1] + hb) & 7)) << 4), b1);
           mma16816<T>(o[n], pa0, pa2, b0[0], b0[1]);
           mma16816<T>(o[n + 1], pa0, pa2, b0[2], b0[3]);
           mma16816<T>(o[n], pb0, pb2, b1[0], b1[1]);
@@ -293,7 +298,10 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       uphase ^= 1;
     }
   }
+  if (a.exp_times && ct == 0) a.exp_times[blockIdx.x * 4 + 3] = gtimer();
 }
+
+unsigned long long* g_exp_times = nullptr;  // EXPERIMENT
 
 constexpr int kMmaNCW = 4;
 constexpr int kMmaRingTarget = 64 * 1024;  // leaves room for 2 CTAs per SM
@@ -312,6 +320,9 @@ int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
   const int st_tok = env_st ? atoi(env_st) : 32;
   const int sb = bs >= st_tok ? 1 : min(4, st_tok / bs);  // stages hold a multiple of 32 tokens
   a.stage_blocks = sb;
+  a.exp_skip = getenv("CLOVE_EXP_SKIP") ? 1 : 0;
+  if (getenv("CLOVE_EXP_TIMES") && !g_exp_times) cudaMalloc(&g_exp_times, 4096 * 4 * 8);
+  a.exp_times = g_exp_times;
   const char* env_ring = getenv("CLOVE_TUNE_RING_KB");
   const int ring_target = env_ring ? atoi(env_ring) * 1024 : kMmaRingTarget;
   const int scratch = kMmaNCW * 8 * (D + 2) * 4;
@@ -364,3 +375,9 @@ template int run_mma<__half, 64>(const clove_pool&, DecodeArgs&, cudaStream_t);
 template int run_mma<__half, 128>(const clove_pool&, DecodeArgs&, cudaStream_t);
 
 }  // namespace clove
+
+// EXPERIMENT: per-CTA timestamps of the last tensor-core decode.
+extern "C" int clove_exp_times(unsigned long long* host, int n) {
+  if (!clove::g_exp_times) return -1;
+  return cudaMemcpy(host, clove::g_exp_times, (size_t)n * 8, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -3;
+}
