@@ -187,12 +187,6 @@ __device__ __forceinline__ int named_bar_or(int id, int nthreads, int pred) {
   return r;
 }
 
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -214,7 +208,6 @@ struct DecodeArgs {
   const int32_t* context_lens;
   float* out;                // [B, Hq, D] f32
   float* partials;           // [B*Hkv, max_chunks, G, D + 2] f32
-  int32_t* counters;         // [B*Hkv]
   const int2* items;         // [n_items] (b, chunk)
   const int32_t* n_items;    // device scalar
   const int32_t* seq_chunks; // [B] chunks per sequence
@@ -233,8 +226,6 @@ struct DecodeArgs {
   int nstage;                // pipeline depth (a multiple of ncw)
   int ncw;                   // consumer warps that take stages (<= the kernel's NCW)
   int stage_blocks;          // blocks per pipeline stage (1..4)
-  int exp_skip;              // EXPERIMENT: consumers skip the math
-  unsigned long long* exp_times;  // EXPERIMENT: per-CTA timestamps (null normally)
   float qscale;              // scale * log2(e)
 };
 
@@ -243,7 +234,6 @@ struct PlanArgs {
   int2* items;
   int32_t* n_items;
   int32_t* seq_chunks;
-  int32_t* counters;
   float* out;
   int32_t* err;
   int batch;
@@ -251,6 +241,7 @@ struct PlanArgs {
   int row_floats;  // Hq * D: output floats per sequence
   int block_size;
   int min_chunk_blocks;      // lower bound on blocks per work item
+  int max_chunk_blocks;      // upper bound (a unit streams at most ~2 MiB of K/V)
   long long target_units;    // work units the chunk size aims for
   int32_t* chunk_blocks;     // out: blocks per work item chosen for this call
   int32_t* unit_counter;     // zeroed: the decode kernel's work-claim counter

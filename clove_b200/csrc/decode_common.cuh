@@ -55,16 +55,16 @@ struct UnitSlot {
 };
 
 // Shared-memory carve-up: [ring: nstage x (K tiles | V tiles)] [barriers]
-// [unit slots] [query buffers] [scratch].  Every region starts 128-byte
+// [unit slots] [query buffers] [2 scratch buffers].  Every region starts 128-byte
 // aligned (bulk tensor copies want 128-byte aligned destinations).
 struct SmemPlan {
   int tile_stride;   // bytes of one [block_size, head_dim] tile, 128-aligned
   int stage_bytes;   // 2 * sb tiles
   int ring_bytes;
-  int bar_bytes;     // full/empty per stage, ufull/uempty per unit slot, misc ints
+  int bar_bytes;     // full/empty per stage, ufull/uempty per unit slot, scr_empty x2, misc ints
   int slot_bytes;    // kUnitRing unit slots
   int q_stride;      // bytes of one query buffer (group * head_dim elements max)
-  int scratch_bytes;
+  int scratch_bytes; // one scratch buffer (consumer-warp states of one unit)
   int total;         // + 128 alignment slack
 };
 
@@ -74,11 +74,11 @@ __host__ __device__ inline SmemPlan smem_plan(int block_size, int head_dim, int 
   s.tile_stride = (block_size * head_dim * elem_bytes + 127) & ~127;
   s.stage_bytes = 2 * sb * s.tile_stride;
   s.ring_bytes = s.stage_bytes * nstage;
-  s.bar_bytes = ((2 * nstage + 2 * kUnitRing) * 8 + 64 + 127) & ~127;
+  s.bar_bytes = ((2 * nstage + 2 * kUnitRing + 2) * 8 + 64 + 127) & ~127;
   s.slot_bytes = (kUnitRing * (int)sizeof(UnitSlot) + 127) & ~127;
   s.q_stride = (q_bytes + 127) & ~127;
   s.scratch_bytes = (scratch_bytes + 127) & ~127;
-  s.total = s.ring_bytes + s.bar_bytes + s.slot_bytes + kUnitRing * s.q_stride + s.scratch_bytes + 128;
+  s.total = s.ring_bytes + s.bar_bytes + s.slot_bytes + kUnitRing * s.q_stride + 2 * s.scratch_bytes + 128;
   return s;
 }
 
@@ -89,10 +89,13 @@ struct SmemPtrs {
   uint64_t* empty;
   uint64_t* ufull;
   uint64_t* uempty;
-  volatile int* misc;  // [0] abort, [1] last-CTA flag
+  uint64_t* scr_empty;  // [2]: scratch buffer free again (arrived by the warp that merged it)
+  volatile int* misc;   // [0] abort
+  int* arrive;          // [2]: consumer warps done with the unit in scratch buffer k
   UnitSlot* slots;
   unsigned char* qbuf;  // kUnitRing x q_stride
-  float* scratch;
+  float* scratch;       // 2 x scratch_floats
+  int scratch_floats;
 };
 
 __device__ __forceinline__ SmemPtrs smem_ptrs(unsigned char* base, const SmemPlan& sp, int nstage) {
@@ -102,15 +105,19 @@ __device__ __forceinline__ SmemPtrs smem_ptrs(unsigned char* base, const SmemPla
   p.empty = p.full + nstage;
   p.ufull = p.empty + nstage;
   p.uempty = p.ufull + kUnitRing;
-  p.misc = reinterpret_cast<volatile int*>(p.uempty + kUnitRing);
+  p.scr_empty = p.uempty + kUnitRing;
+  p.misc = reinterpret_cast<volatile int*>(p.scr_empty + 2);
+  p.arrive = const_cast<int*>(p.misc) + 2;
   p.slots = reinterpret_cast<UnitSlot*>(base + sp.ring_bytes + sp.bar_bytes);
   p.qbuf = base + sp.ring_bytes + sp.bar_bytes + sp.slot_bytes;
   p.scratch = reinterpret_cast<float*>(p.qbuf + kUnitRing * sp.q_stride);
+  p.scratch_floats = sp.scratch_bytes / 4;
   return p;
 }
 
-// Barrier initialisation (thread 0), then a CTA barrier.
-__device__ __forceinline__ void init_barriers(const SmemPtrs& p, int nstage, unsigned long long* a_exp_times = nullptr) {
+// Barrier initialisation (thread 0), then a CTA barrier.  ncw_all: consumer
+// warps in the CTA (each arrives on uempty once per unit).
+__device__ __forceinline__ void init_barriers(const SmemPtrs& p, int nstage, int ncw_all) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < nstage; ++s) {
       mbar_init(&p.full[s], 1);
@@ -118,21 +125,22 @@ __device__ __forceinline__ void init_barriers(const SmemPtrs& p, int nstage, uns
     }
     for (int k = 0; k < kUnitRing; ++k) {
       mbar_init(&p.ufull[k], 1);
-      mbar_init(&p.uempty[k], 1);
+      mbar_init(&p.uempty[k], ncw_all);
     }
+    mbar_init(&p.scr_empty[0], 1);
+    mbar_init(&p.scr_empty[1], 1);
     p.misc[0] = 0;
-    p.misc[1] = 0;
+    p.arrive[0] = 0;
+    p.arrive[1] = 0;
     fence_barrier_init();
   }
   __syncthreads();
-  unsigned long long t0 = gtimer();
   // Launched as a programmatic dependent of the plan kernel: from here on the
   // kernel reads the plan's outputs, so wait for that grid to finish.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (a_exp_times && threadIdx.x == 0) {
-    a_exp_times[blockIdx.x * 4 + 0] = t0;
-    a_exp_times[blockIdx.x * 4 + 1] = gtimer();
-  }
+  // The split-K combine kernel that follows may be scheduled now; it waits
+  // for this grid to finish before it reads anything.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // K tiles of a stage are at [0, sb) * tile_stride, V tiles at
@@ -319,35 +327,41 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
   }
 }
 
-// Consumer side of the unit ring: wait for the next posted unit.  Returns
-// false when the kernel must stop (end marker, or a stuck wait anywhere —
-// all NCT consumer threads agree through the barrier reduction).
-template <int NCT>
-__device__ __forceinline__ bool next_unit(const DecodeArgs& a, const SmemPtrs& sm, int uk, uint32_t uphase,
+// Consumer side of the unit ring: wait (per warp, bounded) for the next
+// posted unit.  Returns false at the end marker or when the kernel must stop
+// (a stuck wait anywhere raises misc[0]; every warp then leaves at its next
+// wait, so no warp is ever left at a barrier).
+__device__ __forceinline__ bool wait_unit(const DecodeArgs& a, const SmemPtrs& sm, int uk, uint32_t uphase,
                                           UnitSlot& out) {
-  const bool ok = !sm.misc[0] && mbar_wait_bounded(&sm.ufull[uk], uphase, a.err);
-  if (!ok) sm.misc[0] = 1;
-  if (named_bar_or(1, NCT, ok ? 0 : 1)) return false;
+  if (sm.misc[0] || !mbar_wait_bounded(&sm.ufull[uk], uphase, a.err)) {
+    sm.misc[0] = 1;
+    return false;
+  }
   out = sm.slots[uk];
   return out.valid != 0;
 }
 
-// Epilogue of one unit, run by all NCT consumer threads (ct in [0, NCT)).
-// scratch holds NW partial softmax states [NW][G][D + 2] = (acc[D], m, l) in
-// the log2 domain.  A sequence in one chunk is finished here; otherwise the
-// merged chunk state goes to the workspace partials and the CTA that finishes
-// the last chunk of (b, h) — found with an atomic counter, no waiting —
-// merges all chunks and writes the output.
-template <int D, int G, int NW, int NCT>
-__device__ void finish_unit(const DecodeArgs& a, const Unit& x, int nchunks, const float* scratch,
-                            volatile int* s_last, int ct) {
+__device__ __forceinline__ bool wait_or_abort(const DecodeArgs& a, const SmemPtrs& sm, uint64_t* bar,
+                                              uint32_t parity) {
+  if (sm.misc[0] || !mbar_wait_bounded(bar, parity, a.err)) {
+    sm.misc[0] = 1;
+    return false;
+  }
+  return true;
+}
+
+// Merge the NW consumer-warp states of one unit (scratch [NW][G][D + 2] =
+// (acc[D], m, l), log2 domain), run by one warp.  A sequence in one chunk is
+// finished here; otherwise the merged chunk state goes to the workspace
+// partials [B*Hkv, max_chunks, group, D + 2] and the combine kernel finishes
+// the sequence.
+template <int D, int G, int NW>
+__device__ void merge_unit(const DecodeArgs& a, const Unit& x, int nchunks, const float* scratch, int lane) {
   const int group = a.group;
   const int Hkv = a.num_kv_heads;
   const int Hq = Hkv * group;
-  // Partials [B*Hkv, max_chunks, group, D + 2], indexed by the runtime group
-  // (the workspace is sized by it, not by the kernel's row capacity G).
   float* part_base = a.partials + (((size_t)x.b * Hkv + x.h) * a.max_chunks) * group * (D + 2);
-  for (int idx = ct; idx < group * D; idx += NCT) {
+  for (int idx = lane; idx < group * D; idx += 32) {
     const int g = idx / D, d = idx - (idx / D) * D;
     float M = -INFINITY;
 #pragma unroll
@@ -373,31 +387,30 @@ __device__ void finish_unit(const DecodeArgs& a, const Unit& x, int nchunks, con
       }
     }
   }
-  if (nchunks > 1) {
-    __threadfence();
-    named_bar_sync(1, NCT);
-    if (ct == 0) {
-      const int prev = atomicAdd(a.counters + (size_t)x.b * Hkv + x.h, 1);
-      *s_last = (prev == nchunks - 1);
-    }
-    named_bar_sync(1, NCT);
-    if (*s_last) {
-      __threadfence();
-      for (int idx = ct; idx < group * D; idx += NCT) {
-        const int g = idx / D, d = idx - (idx / D) * D;
-        float M = -INFINITY;
-        for (int cc = 0; cc < nchunks; ++cc)
-          M = fmaxf(M, __ldcg(part_base + ((size_t)cc * group + g) * (D + 2) + D));
-        float Ls = 0.f, O = 0.f;
-        for (int cc = 0; cc < nchunks; ++cc) {
-          const float* P = part_base + ((size_t)cc * group + g) * (D + 2);
-          const float f = exp2f(__ldcg(P + D) - M);
-          Ls = fmaf(__ldcg(P + D + 1), f, Ls);
-          O = fmaf(__ldcg(P + d), f, O);
-        }
-        a.out[((size_t)x.b * Hq + (size_t)x.h * group + g) * D + d] = O / Ls;
-      }
-      if (ct == 0) a.counters[(size_t)x.b * Hkv + x.h] = 0;
+}
+
+// Unit hand-off, run by every consumer warp after it wrote its state into
+// scratch buffer sbuf: release the unit slot, count the warp in, and if it
+// is the last of the NW warps, merge the unit and free the buffer.  No warp
+// waits for another here.
+template <int D, int G, int NW>
+__device__ __forceinline__ void hand_off(const DecodeArgs& a, const SmemPtrs& sm, const UnitSlot& us, int sbuf,
+                                         int uk, int lane) {
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    __threadfence_block();
+    last = atomicAdd(&sm.arrive[sbuf], 1) == NW - 1;
+    mbar_arrive(&sm.uempty[uk]);  // this warp no longer reads the unit's slot
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (last) {
+    __threadfence_block();
+    merge_unit<D, G, NW>(a, us.x, us.nchunks, sm.scratch + sbuf * sm.scratch_floats, lane);
+    __syncwarp();
+    if (lane == 0) {
+      sm.arrive[sbuf] = 0;
+      mbar_arrive(&sm.scr_empty[sbuf]);
     }
   }
 }

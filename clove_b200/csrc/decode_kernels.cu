@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
   __syncthreads();
   auto len_of = [&](int b) { return b == b0 ? L0 : clamp_ctx(p.context_lens, b, p.max_ctx, p.append); };
   // Chunk size from the actual work: total (block, KV head) pairs spread
-  // over ~target_units work items, never below min_chunk_blocks.
+  // over ~target_units work items, capped at max_chunk_blocks, never below
+  // min_chunk_blocks.
   {
     long long mine = 0;
     for (int b = tid; b < p.batch; b += kPlanThreads) mine += (len_of(b) + p.block_size - 1) / p.block_size;
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
   }
   __syncthreads();
   const long long want = (s_blocks * p.num_kv_heads + p.target_units - 1) / p.target_units;
-  const int cb = (int)max((long long)p.min_chunk_blocks, want);
+  const int cb = (int)max((long long)p.min_chunk_blocks, min((long long)p.max_chunk_blocks, want));
   if (tid == 0) *p.chunk_blocks = cb;
 
   // pass 1: per-sequence bookkeeping, full chunks, partial-size histogram
@@ -129,7 +130,6 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
       nfull = nbl / cb;
       const int rem = nbl - nfull * cb;
       p.seq_chunks[b] = nfull + (rem > 0);
-      for (int h = 0; h < p.num_kv_heads; ++h) p.counters[(size_t)b * p.num_kv_heads + h] = 0;
       if (rem > 0) atomicAdd(&hist[(rem - 1) * kPlanBins / cb], 1);
       if (L == 0) {
         float* row = p.out + (size_t)b * p.row_floats;
@@ -205,18 +205,15 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   const int DL = D / LPT;
   const int CH = DL / EPC;
   const int group = a.group;
-  const int Hq = a.num_kv_heads * group;
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const SmemPlan sp = smem_plan(bs, D, (int)sizeof(T), sb, a.nstage,
-                                (NCW * G * (D + 2) + G * D) * (int)sizeof(float), G * D * (int)sizeof(T));
+                                NCW * G * (D + 2) * (int)sizeof(float), G * D * (int)sizeof(T));
   const SmemPtrs sm = smem_ptrs(smem, sp, a.nstage);
-  float* scratch = sm.scratch;
-  float* qs = scratch + NCW * G * (D + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  init_barriers(sm, a.nstage);
+  init_barriers(sm, a.nstage, NCW);
   const int n_units = *a.n_items * a.num_kv_heads;
 
   if (warp == 0) {
@@ -225,22 +222,16 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   }
 
   const int cw = warp - 1;
-  const int ct = threadIdx.x - 32;
   const int tk_l = lane / LPT;    // token of this lane within a pass
   const int part = lane % LPT;    // which D/LPT slice of that token
   int gbase = 0;                  // stages of earlier units (CTA-wide count)
-  float* my_scr = scratch + (size_t)cw * G * (D + 2);
-  int uk = 0;
+  int uk = 0, n_done = 0;
   uint32_t uphase = 0;
   UnitSlot us;
 
-  while (next_unit<NCT>(a, sm, uk, uphase, us)) {
+  while (wait_unit(a, sm, uk, uphase, us)) {
     const Unit x = us.x;
-    {
-      const T* qg = reinterpret_cast<const T*>(sm.qbuf + uk * sp.q_stride);
-      for (int i = ct; i < group * D; i += NCT) qs[i] = Elem<T>::to_f(qg[i]) * a.qscale;
-    }
-    named_bar_sync(1, NCT);
+    const T* qs = reinterpret_cast<const T*>(sm.qbuf + uk * sp.q_stride);  // the unit's raw query rows
 
     float m[G], l[G], acc[G][E];
 #pragma unroll
@@ -276,7 +267,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
 #pragma unroll
         for (int g = 0; g < G; ++g) s[g] = 0.f;
         const T* krow = Ks + (size_t)tk * D + part * DL;
-        const float* qrow = qs + part * DL;
+        const T* qrow = qs + part * DL;
         for (int c = 0; c < CH; ++c) {
           const int cc = (c + lane) & (CH - 1);
           float kf[EPC];
@@ -284,15 +275,10 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
 #pragma unroll
           for (int g = 0; g < G; ++g) {
             if (g < group) {
-              const float4* q4 = reinterpret_cast<const float4*>(qrow + g * D + cc * EPC);
+              float qf[EPC];
+              load_vec_f32<T, EPC>(qrow + g * D + cc * EPC, qf);
 #pragma unroll
-              for (int v4 = 0; v4 < EPC / 4; ++v4) {
-                const float4 qq = q4[v4];
-                s[g] = fmaf(qq.x, kf[4 * v4 + 0], s[g]);
-                s[g] = fmaf(qq.y, kf[4 * v4 + 1], s[g]);
-                s[g] = fmaf(qq.z, kf[4 * v4 + 2], s[g]);
-                s[g] = fmaf(qq.w, kf[4 * v4 + 3], s[g]);
-              }
+              for (int e = 0; e < EPC; ++e) s[g] = fmaf(qf[e], kf[e], s[g]);
             }
           }
         }
@@ -300,7 +286,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           for (int o = 1; o < LPT; o <<= 1) s[g] += __shfl_xor_sync(0xffffffffu, s[g], o);
-          s[g] = valid ? s[g] : -INFINITY;
+          s[g] = valid ? s[g] * a.qscale : -INFINITY;
         }
         // ---- online softmax (warp-uniform max / correction) ----
         float pe[G];
@@ -335,12 +321,13 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.empty[slot]);
     }
-    // A consumer warp that met a stuck wait stops here; the reduction keeps
-    // every consumer thread on the same path (no one is left at a barrier).
-    if (named_bar_or(1, NCT, aborted ? 1 : 0)) return;
+    if (aborted) return;  // the abort flag is up; every other warp leaves at its next wait
     gbase += x.nstages;
 
-    // ---- publish this warp's state, merge, finish ----
+    // ---- publish this warp's state (double-buffered scratch), hand off ----
+    const int sbuf = n_done & 1;
+    if (!wait_or_abort(a, sm, &sm.scr_empty[sbuf], ((uint32_t)(n_done >> 1) & 1u) ^ 1u)) return;
+    float* my_scr = sm.scratch + sbuf * sm.scratch_floats + (size_t)cw * G * (D + 2);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float lsum = warp_sum(l[g]);
@@ -351,14 +338,48 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         my_scr[g * (D + 2) + D + 1] = lsum;
       }
     }
-    named_bar_sync(1, NCT);
-    finish_unit<D, G, NCW, NCT>(a, x, us.nchunks, scratch, &sm.misc[1], ct);
-    named_bar_sync(1, NCT);  // scratch, q and misc[1] are reused by the next unit
-    if (ct == 0) mbar_arrive(&sm.uempty[uk]);
+    hand_off<D, G, NCW>(a, sm, us, sbuf, uk, lane);
+    ++n_done;
     if (++uk == kUnitRing) {
       uk = 0;
       uphase ^= 1;
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// split-K combine
+// ---------------------------------------------------------------------------
+// One CTA per (sequence, query head): for a sequence the decode split into
+// several chunks, merge the chunk states (m, l, acc) of the partials with a
+// log-sum-exp combine and write the output row.  Sequences in one chunk were
+// finished by the decode kernel; their CTAs exit at once.  Launched as a
+// programmatic dependent of the decode kernel.
+__global__ void __launch_bounds__(128) combine_kernel(const DecodeArgs a, int head_dim) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int group = a.group;
+  const int Hq = a.num_kv_heads * group;
+  const int b = blockIdx.x / Hq, hq = blockIdx.x - (blockIdx.x / Hq) * Hq;
+  const int nchunks = a.seq_chunks[b];
+  if (nchunks <= 1) return;
+  const int h = hq / group, g = hq - h * group;
+  const int D = head_dim;
+  const float* base = a.partials + (((size_t)b * a.num_kv_heads + h) * a.max_chunks) * group * (D + 2);
+  float M = -INFINITY;
+  for (int c = 0; c < nchunks; ++c) M = fmaxf(M, base[((size_t)c * group + g) * (D + 2) + D]);
+  float Ls = 0.f;
+  for (int c = 0; c < nchunks; ++c) {
+    const float* P = base + ((size_t)c * group + g) * (D + 2);
+    Ls = fmaf(P[D + 1], exp2f(P[D] - M), Ls);
+  }
+  const float inv = 1.f / Ls;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float O = 0.f;
+    for (int c = 0; c < nchunks; ++c) {
+      const float* P = base + ((size_t)c * group + g) * (D + 2);
+      O = fmaf(P[d], exp2f(P[D] - M), O);
+    }
+    a.out[((size_t)b * Hq + hq) * D + d] = O * inv;
   }
 }
 
@@ -391,8 +412,6 @@ DecodeLayout decode_layout(const clove_pool& pool, int batch, int num_q_heads, i
   off = align256(off + sizeof(int2) * (size_t)batch * L.max_chunks);
   L.off_seq_chunks = off;
   off = align256(off + sizeof(int32_t) * (size_t)batch);
-  L.off_counters = off;
-  off = align256(off + sizeof(int32_t) * (size_t)batch * hkv);
   L.off_partials = off;
   // Partials are only written when a sequence spans more than one chunk.
   if (L.max_chunks > 1)
@@ -407,7 +426,7 @@ static int run_simt(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) 
   const int bs = pool.block_size;
   const int sb = bs >= 16 ? 1 : 16 / bs;
   a.stage_blocks = sb;
-  const int scratch = (kNCW * G * (D + 2) + G * D) * 4;
+  const int scratch = kNCW * G * (D + 2) * 4;
   const int qb = G * D * (int)sizeof(T);
   SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb);
   // nstage: a multiple of the number of consumer warps that take stages (see
@@ -500,7 +519,6 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   p.items = reinterpret_cast<int2*>(ws + L.off_items);
   p.n_items = reinterpret_cast<int32_t*>(ws + L.off_nitems);
   p.seq_chunks = reinterpret_cast<int32_t*>(ws + L.off_seq_chunks);
-  p.counters = reinterpret_cast<int32_t*>(ws + L.off_counters);
   p.out = call.out;
   p.err = reinterpret_cast<int32_t*>(ws + L.off_err);
   p.batch = call.batch;
@@ -508,7 +526,10 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   p.row_floats = call.num_q_heads * pool.head_dim;
   p.block_size = pool.block_size;
   p.min_chunk_blocks = L.chunk_blocks;
-  p.target_units = (long long)pool.num_sms * 4;  // ~2 units per resident CTA (measured best on C2-C5)
+  // ~2 units per resident CTA, and no unit above ~2 MiB of K/V, so the tail
+  // (the last units still streaming) stays short (measured on c2-c5).
+  p.target_units = (long long)pool.num_sms * 4;
+  p.max_chunk_blocks = (int)((2u << 20) / (2u * pool.block_size * pool.head_dim * pool.elem_bytes));
   p.chunk_blocks = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 1;
   p.unit_counter = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 2;
   p.max_ctx = call.max_ctx;
@@ -531,7 +552,6 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   a.context_lens = call.context_lens;
   a.out = call.out;
   a.partials = reinterpret_cast<float*>(ws + L.off_partials);
-  a.counters = p.counters;
   a.items = p.items;
   a.n_items = p.n_items;
   a.seq_chunks = p.seq_chunks;
@@ -548,19 +568,38 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   a.group = call.num_q_heads / pool.num_kv_heads;
   a.append = append;
   a.nstage = 2;
-  a.exp_skip = 0;
-  a.exp_times = nullptr;
   a.ncw = 1;
   a.qscale = call.scale * kLog2e;
 
+  int rc;
   switch (pool.dtype) {
-    case CLOVE_DTYPE_F32: return dispatch_dim<float>(pool, a, stream);
-    case CLOVE_DTYPE_BF16: return dispatch_dim<__nv_bfloat16>(pool, a, stream);
-    case CLOVE_DTYPE_F16: return dispatch_dim<__half>(pool, a, stream);
+    case CLOVE_DTYPE_F32: rc = dispatch_dim<float>(pool, a, stream); break;
+    case CLOVE_DTYPE_BF16: rc = dispatch_dim<__nv_bfloat16>(pool, a, stream); break;
+    case CLOVE_DTYPE_F16: rc = dispatch_dim<__half>(pool, a, stream); break;
     default:
       set_last_error("paged_decode: dtype %d", pool.dtype);
       return CLOVE_ERR_UNSUPPORTED;
   }
+  if (rc != CLOVE_OK || L.max_chunks <= 1) return rc;
+  // Split-K combine for the sequences the plan split into several chunks.
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(call.batch * call.num_q_heads));
+    cfg.blockDim = dim3(128);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, combine_kernel, a, pool.head_dim);
+    if (e != cudaSuccess) {
+      set_last_error("combine launch: %s", cudaGetErrorString(e));
+      return CLOVE_ERR_CUDA;
+    }
+    count_launches(1);
+  }
+  return CLOVE_OK;
 }
 
 }  // namespace clove

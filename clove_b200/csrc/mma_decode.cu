@@ -24,8 +24,6 @@
 #include "host.h"
 #include "mma_decode.cuh"
 
-#include <cstdlib>
-
 namespace clove {
 
 template <typename T> struct MmaType;
@@ -114,7 +112,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
                                 G * D * (int)sizeof(T));
   const SmemPtrs sm = smem_ptrs(smem, sp, a.nstage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  init_barriers(sm, a.nstage, a.exp_times);
+  init_barriers(sm, a.nstage, NCW);
   const int n_units = *a.n_items * a.num_kv_heads;
 
   if (warp == 0) {
@@ -123,19 +121,17 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   }
 
   const int cw = warp - 1;
-  const int ct = threadIdx.x - 32;
   const int g = lane >> 2;      // query row of this lane's fragment values
   const int tq = lane & 3;      // column pair within an 8-wide n-tile
   const int mi = lane >> 3;     // ldmatrix: which 8x8 matrix this lane addresses
   const int mr = lane & 7;      // ldmatrix: which row of it
   const float sl2 = a.qscale;   // scale * log2(e), applied to the f32 scores
   int gbase = 0;
-  float* my_scr = sm.scratch + (size_t)cw * G * (D + 2);
-  int uk = 0;
+  int uk = 0, n_done = 0;
   uint32_t uphase = 0;
   UnitSlot us;
 
-  while (next_unit<NCT>(a, sm, uk, uphase, us)) {
+  while (wait_unit(a, sm, uk, uphase, us)) {
     const Unit x = us.x;
     // Q fragments (A operand rows = query heads of this KV head), unscaled,
     // from the unit's query buffer.
@@ -170,7 +166,6 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         aborted = true;
         break;
       }
-      if (a.exp_times && gs == 0 && lane == 0) a.exp_times[blockIdx.x * 4 + 2] = gtimer();
       unsigned char* kst = sm.ring + (size_t)slot * sp.stage_bytes;
       unsigned char* vst = kst + sb * sp.tile_stride;
       const int ntok = min(TT, x.L - (x.blk0 + j * sb) * bs);
@@ -185,7 +180,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       }
       const uint32_t kbase = smem_u32(kst), vbase = smem_u32(vst);
       constexpr int NH = D / 64;  // 128-byte rows per token
-      for (int p0 = 0; p0 < (a.exp_skip ? 0 : ntok); p0 += 32) {
+      for (int p0 = 0; p0 < ntok; p0 += 32) {
         // 32 tokens per pass, as two 16-token halves h = 0, 1.  Per-pass
         // ldmatrix row addresses: chunk ch of token tok lives at
         // tile_off(tok) + row * 128 + (((ch & 7) ^ (row & 7)) << 4), with
@@ -272,12 +267,15 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.empty[slot]);
     }
-    if (named_bar_or(1, NCT, aborted ? 1 : 0)) return;
+    if (aborted) return;  // the abort flag is up; every other warp leaves at its next wait
     gbase += x.nstages;
 
-    // ---- publish (acc, m, l) of rows g < group; rows of idle warps stay -inf ----
+    // ---- publish (acc, m, l) of rows g < group (double-buffered scratch), hand off ----
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const int sbuf = n_done & 1;
+    if (!wait_or_abort(a, sm, &sm.scr_empty[sbuf], ((uint32_t)(n_done >> 1) & 1u) ^ 1u)) return;
+    float* my_scr = sm.scratch + sbuf * sm.scratch_floats + (size_t)cw * G * (D + 2);
     if (g < group) {
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
@@ -289,19 +287,14 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
         my_scr[g * (D + 2) + D + 1] = l;
       }
     }
-    named_bar_sync(1, NCT);
-    finish_unit<D, G, NCW, NCT>(a, x, us.nchunks, sm.scratch, &sm.misc[1], ct);
-    named_bar_sync(1, NCT);
-    if (ct == 0) mbar_arrive(&sm.uempty[uk]);
+    hand_off<D, G, NCW>(a, sm, us, sbuf, uk, lane);
+    ++n_done;
     if (++uk == kUnitRing) {
       uk = 0;
       uphase ^= 1;
     }
   }
-  if (a.exp_times && ct == 0) a.exp_times[blockIdx.x * 4 + 3] = gtimer();
 }
-
-unsigned long long* g_exp_times = nullptr;  // EXPERIMENT
 
 constexpr int kMmaNCW = 4;
 constexpr int kMmaRingTarget = 64 * 1024;  // leaves room for 2 CTAs per SM
@@ -316,20 +309,13 @@ int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
   const int bs = pool.block_size;
   // Stages of >= 32 tokens: fixed per-stage costs (barrier round trips, copy
   // issue) halve against 16-token stages.
-  const char* env_st = getenv("CLOVE_TUNE_STAGE_TOKENS");
-  const int st_tok = env_st ? atoi(env_st) : 32;
-  const int sb = bs >= st_tok ? 1 : min(4, st_tok / bs);  // stages hold a multiple of 32 tokens
+  const int sb = bs >= 32 ? 1 : 32 / bs;  // stages hold a multiple of 32 tokens
   a.stage_blocks = sb;
-  a.exp_skip = getenv("CLOVE_EXP_SKIP") ? 1 : 0;
-  if (getenv("CLOVE_EXP_TIMES") && !g_exp_times) cudaMalloc(&g_exp_times, 4096 * 4 * 8);
-  a.exp_times = g_exp_times;
-  const char* env_ring = getenv("CLOVE_TUNE_RING_KB");
-  const int ring_target = env_ring ? atoi(env_ring) * 1024 : kMmaRingTarget;
   const int scratch = kMmaNCW * 8 * (D + 2) * 4;
   const int qb = 8 * D * (int)sizeof(T);
   SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb);
   int ncw = kMmaNCW;
-  int nstage = (ring_target / sp.stage_bytes) / ncw * ncw;
+  int nstage = (kMmaRingTarget / sp.stage_bytes) / ncw * ncw;
   if (nstage < ncw) nstage = ncw;
   if (nstage > 4 * ncw) nstage = 4 * ncw;
   sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);
@@ -375,9 +361,3 @@ template int run_mma<__half, 64>(const clove_pool&, DecodeArgs&, cudaStream_t);
 template int run_mma<__half, 128>(const clove_pool&, DecodeArgs&, cudaStream_t);
 
 }  // namespace clove
-
-// EXPERIMENT: per-CTA timestamps of the last tensor-core decode.
-extern "C" int clove_exp_times(unsigned long long* host, int n) {
-  if (!clove::g_exp_times) return -1;
-  return cudaMemcpy(host, clove::g_exp_times, (size_t)n * 8, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -3;
-}

@@ -15,7 +15,7 @@
 //     rejected with CLOVE_ERR_WORKSPACE.
 //   - Every call on a GPU shares the one array and it keeps what the last
 //     call left there; the plan kernel of each call re-initialises everything
-//     the decode reads from it (counters, item list, check flags).  Calls
+//     the decode reads from it (item list, claim counter, check flags).  Calls
 //     that overlap on the GPU (other streams, other host threads) race on it:
 //     serialise them.
 //   - The first call on a device looks up the array's device address (with
