@@ -203,21 +203,25 @@ def run_ours(args) -> None:
         _, kn, vn, _ = fill_values(llay, dev, pool.storage)
         gq = torch.Generator(device=dev)
         gq.manual_seed(spec.seed)
-        q = torch.randn((lay.batch, spec.num_q_heads, spec.head_dim), generator=gq, device=dev).to(spec.dtype)
+        q_all = torch.randn((lay.batch, spec.num_q_heads, spec.head_dim), generator=gq, device=dev).to(spec.dtype)
+        hl = spec.num_q_heads // ws
+        q = q_all[:, rank * hl:(rank + 1) * hl].contiguous()  # this rank's query heads
+        gbuf = torch.empty((ws * lay.batch, hl, spec.head_dim), dtype=torch.float32, device=dev)
     else:
         lay = make_layout(spec, seed=spec.seed + rank, batch=args.batch)
         pool = KVPool(lay.num_blocks, spec.block_size, spec.num_kv_heads, spec.head_dim, spec.dtype, dev)
         q, kn, vn, _ = fill_values(lay, dev, pool.storage)
     bt = torch.from_numpy(lay.block_tables).to(dev)
     cl = torch.from_numpy(lay.context_lens).to(dev)
-    out = torch.empty((lay.batch, spec.num_q_heads, spec.head_dim), dtype=torch.float32, device=dev)
+    out = torch.empty((lay.batch, q.shape[1], spec.head_dim), dtype=torch.float32, device=dev)
     max_ctx = lay.max_ctx
     stream = torch.cuda.current_stream(dev)
 
     def step():
+        # launches on the current stream (the capture stream while a graph is recorded)
         if head_split:
-            return head_sharded_append_decode(pool, q, kn, vn, bt, cl, ws, rank, max_ctx)
-        return pool.append_decode(q, kn, vn, bt, cl, max_ctx=max_ctx, out=out, stream=stream)
+            return head_sharded_append_decode(pool, q, kn, vn, bt, cl, ws, max_ctx, out_local=out, gather_buf=gbuf)
+        return pool.append_decode(q, kn, vn, bt, cl, max_ctx=max_ctx, out=out)
 
     def barrier():
         if ws > 1:
@@ -226,22 +230,36 @@ def run_ours(args) -> None:
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
-    if pool.decode_status(lay.batch, spec.num_q_heads, max_ctx) != 0:
+    if pool.decode_status(lay.batch, q.shape[1], max_ctx) != 0:
         raise RuntimeError("device check flags raised on the bench workload")
+    n0 = launch_count()
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = launch_count() - n0
+    # One step captured in a CUDA graph and replayed: the timed region then
+    # holds only device work (plan, decode, combine, and the all-gather under
+    # head sharding), not Python launch overhead.
+    run = step
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+        run = graph.replay
 
     # ---- device-timed region: inputs resident in HBM ----
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    n0 = launch_count()
     with ClockSampler(local) as clocks:
         ev0.record(stream)
         for _ in range(args.steps):
-            step()
+            run()
         ev1.record(stream)
         torch.cuda.synchronize()
     barrier()
-    launches = launch_count() - n0
+    launches = launches_per_step * args.steps
     ms = ev0.elapsed_time(ev1) / args.steps
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if ws > 1:
@@ -252,7 +270,8 @@ def run_ours(args) -> None:
     hq = q.cpu().pin_memory()
     hk, hv = kn.cpu().pin_memory(), vn.cpu().pin_memory()
     hbt, hcl = bt.cpu().pin_memory(), cl.cpu().pin_memory()
-    hout = torch.empty(out.shape, dtype=torch.float32).pin_memory()
+    hout = torch.empty((lay.batch, ws, out.shape[1], spec.head_dim) if head_split else out.shape,
+                       dtype=torch.float32).pin_memory()
     dq, dk, dv, dbt, dcl = (torch.empty_like(x, device=dev) for x in (hq, hk, hv, hbt, hcl))
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hbt, hcl))
     d2h = hout.numel() * 4
@@ -261,7 +280,8 @@ def run_ours(args) -> None:
         def e2e_step():
             for d, h in ((dq, hq), (dk, hk), (dv, hv), (dbt, hbt), (dcl, hcl)):
                 d.copy_(h, non_blocking=True)
-            res = head_sharded_append_decode(pool, dq, dk, dv, dbt, dcl, ws, rank, max_ctx)
+            res = head_sharded_append_decode(pool, dq, dk, dv, dbt, dcl, ws, max_ctx, out_local=out,
+                                             gather_buf=gbuf)
             hout.copy_(res, non_blocking=True)
     else:
         # Through the reference-facing FFI (include/clove_ffi.h): tensors made
@@ -353,6 +373,7 @@ def main() -> None:
     ap.add_argument("--config", default="c2")
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--batch", type=int, default=None, help="override the config batch (profiling only)")
+    ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a captured CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per decode launch from an ncu capture (reported as roofline.traffic)")

@@ -355,7 +355,13 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
 // log-sum-exp combine and write the output row.  Sequences in one chunk were
 // finished by the decode kernel; their CTAs exit at once.  Launched as a
 // programmatic dependent of the decode kernel.
-__global__ void __launch_bounds__(128) combine_kernel(const DecodeArgs a, int head_dim) {
+constexpr int kCombineThreads = 128;
+constexpr int kCombineMaxChunks = 2048;  // chunk weights staged in shared memory
+
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeArgs a, int head_dim) {
+  __shared__ float w[kCombineMaxChunks];
+  __shared__ float red[kCombineThreads / 32];
+  __shared__ float s_bcast;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int group = a.group;
   const int Hq = a.num_kv_heads * group;
@@ -364,22 +370,53 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeArgs a, int he
   if (nchunks <= 1) return;
   const int h = hq / group, g = hq - h * group;
   const int D = head_dim;
-  const float* base = a.partials + (((size_t)b * a.num_kv_heads + h) * a.max_chunks) * group * (D + 2);
-  float M = -INFINITY;
-  for (int c = 0; c < nchunks; ++c) M = fmaxf(M, base[((size_t)c * group + g) * (D + 2) + D]);
-  float Ls = 0.f;
-  for (int c = 0; c < nchunks; ++c) {
-    const float* P = base + ((size_t)c * group + g) * (D + 2);
-    Ls = fmaf(P[D + 1], exp2f(P[D] - M), Ls);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const size_t cstride = (size_t)group * (D + 2);  // floats between consecutive chunks
+  const float* base = a.partials + (((size_t)b * a.num_kv_heads + h) * a.max_chunks * group + g) * (D + 2);
+  const int nc = min(nchunks, kCombineMaxChunks);  // the plan never exceeds this (see decode_layout)
+  // 1. M = max_c m_c  (block reduction)
+  float mx = -INFINITY;
+  for (int c = tid; c < nc; c += kCombineThreads) mx = fmaxf(mx, base[c * cstride + D]);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float m = red[0];
+    for (int i = 1; i < kCombineThreads / 32; ++i) m = fmaxf(m, red[i]);
+    s_bcast = m;
   }
-  const float inv = 1.f / Ls;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float O = 0.f;
-    for (int c = 0; c < nchunks; ++c) {
-      const float* P = base + ((size_t)c * group + g) * (D + 2);
-      O = fmaf(P[d], exp2f(P[D] - M), O);
+  __syncthreads();
+  const float M = s_bcast;
+  // 2. w_c = 2^(m_c - M); L = sum_c w_c l_c
+  float ls = 0.f;
+  for (int c = tid; c < nc; c += kCombineThreads) {
+    const float wc = exp2f(base[c * cstride + D] - M);
+    w[c] = wc;
+    ls = fmaf(wc, base[c * cstride + D + 1], ls);
+  }
+  for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = ls;
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.f;
+    for (int i = 0; i < kCombineThreads / 32; ++i) t += red[i];
+    s_bcast = 1.f / t;
+  }
+  __syncthreads();
+  const float inv = s_bcast;
+  // 3. out[d] = inv * sum_c w_c acc_c[d]: loads coalesced over d, independent over c
+  for (int d = tid; d < D; d += kCombineThreads) {
+    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+    int c = 0;
+    for (; c + 4 <= nc; c += 4) {
+      o0 = fmaf(w[c], base[c * cstride + d], o0);
+      o1 = fmaf(w[c + 1], base[(c + 1) * cstride + d], o1);
+      o2 = fmaf(w[c + 2], base[(c + 2) * cstride + d], o2);
+      o3 = fmaf(w[c + 3], base[(c + 3) * cstride + d], o3);
     }
-    a.out[((size_t)b * Hq + hq) * D + d] = O * inv;
+    for (; c < nc; ++c) o0 = fmaf(w[c], base[c * cstride + d], o0);
+    a.out[((size_t)b * Hq + hq) * D + d] = ((o0 + o1) + (o2 + o3)) * inv;
   }
 }
 
@@ -400,8 +437,10 @@ DecodeLayout decode_layout(const clove_pool& pool, int batch, int num_q_heads, i
   DecodeLayout L;
   const int hkv = pool.num_kv_heads;
   const int group = num_q_heads / hkv;
-  L.chunk_blocks = min_chunk_blocks(pool.block_size);
   const int max_blocks = (max_ctx + pool.block_size - 1) / pool.block_size;
+  // Smallest chunk: 256 tokens, and few enough chunks per sequence for the
+  // combine kernel's shared-memory weights.
+  L.chunk_blocks = max(min_chunk_blocks(pool.block_size), (max_blocks + kCombineMaxChunks - 1) / kCombineMaxChunks);
   L.max_chunks = max_blocks <= 0 ? 1 : (max_blocks + L.chunk_blocks - 1) / L.chunk_blocks;
   size_t off = 0;
   L.off_err = off;
@@ -585,7 +624,7 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(call.batch * call.num_q_heads));
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(kCombineThreads);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -54,17 +54,24 @@ def gather_heads(out_local: torch.Tensor, world: int, group_pg=None) -> torch.Te
     return buf.view(world, B, hl, D).permute(1, 0, 2, 3).reshape(B, world * hl, D)
 
 
-def head_sharded_append_decode(pool_local, q: torch.Tensor, k_new_local: torch.Tensor,
+def head_sharded_append_decode(pool_local, q_local: torch.Tensor, k_new_local: torch.Tensor,
                                v_new_local: torch.Tensor, block_tables: torch.Tensor,
-                               context_lens: torch.Tensor, world: int, rank: int, max_ctx: int,
-                               scale: float | None = None) -> torch.Tensor:
-    """Append + decode under KV-head sharding.  q: [B, Hq, D] (all heads);
-    pool_local / k_new_local / v_new_local hold this rank's KV heads only.
-    Returns the full [B, Hq, D] output on every rank."""
-    B, hq, D = q.shape
-    group = hq // (pool_local.num_kv_heads * world)
-    _, qh = local_heads(pool_local.num_kv_heads * world, group, world, rank)
-    q_local = q[:, qh.start:qh.stop].contiguous()
+                               context_lens: torch.Tensor, world: int, max_ctx: int,
+                               scale: float | None = None, out_local: torch.Tensor | None = None,
+                               gather_buf: torch.Tensor | None = None) -> torch.Tensor:
+    """Append + decode under KV-head sharding.  Every argument is this rank's
+    share: q_local [B, hq_local, D] holds the query heads of the KV heads in
+    pool_local (rank r: query heads r*hq_local .. (r+1)*hq_local - 1, as
+    local_heads gives them), k_new_local / v_new_local [B, hkv_local, D].
+    Returns the full [B, world*hq_local, D] output on every rank.
+    Preallocated out_local / gather_buf make the call free of allocations
+    (e.g. for CUDA-graph capture)."""
     out_local = pool_local.append_decode(q_local, k_new_local, v_new_local, block_tables, context_lens,
-                                         scale=scale, max_ctx=max_ctx)
-    return gather_heads(out_local, world)
+                                         scale=scale, max_ctx=max_ctx, out=out_local)
+    if world == 1:
+        return out_local
+    B, hl, D = out_local.shape
+    if gather_buf is None:
+        gather_buf = torch.empty((world * B, hl, D), dtype=out_local.dtype, device=out_local.device)
+    dist.all_gather_into_tensor(gather_buf, out_local)
+    return gather_buf.view(world, B, hl, D).permute(1, 0, 2, 3)  # [B, world, hl, D] view

@@ -33,13 +33,15 @@ def _worker(rank, world, port, q_out):
     lay = make_layout(spec)
     full = KVPool(lay.num_blocks, 32, 4, 128, torch.bfloat16, dev)
     q, kn, vn, _ = fill_values(lay, dev, full.storage)  # same seed: identical on every rank
-    kvh, _ = local_heads(4, 4, world, rank)
+    kvh, qh = local_heads(4, 4, world, rank)
     local = KVPool(lay.num_blocks, 32, kvh.stop - kvh.start, 128, torch.bfloat16, dev,
                    storage=full.storage[:, :, :, kvh.start:kvh.stop].contiguous())
     bt = torch.from_numpy(lay.block_tables).to(dev)
     cl = torch.from_numpy(lay.context_lens).to(dev)
-    got = head_sharded_append_decode(local, q, kn[:, kvh.start:kvh.stop].contiguous(),
-                                     vn[:, kvh.start:kvh.stop].contiguous(), bt, cl, world, rank, lay.max_ctx)
+    got = head_sharded_append_decode(local, q[:, qh.start:qh.stop].contiguous(),
+                                     kn[:, kvh.start:kvh.stop].contiguous(),
+                                     vn[:, kvh.start:kvh.stop].contiguous(), bt, cl, world, lay.max_ctx)
+    got = got.reshape(q.shape[0], q.shape[1], q.shape[2])
     ref = full.append_decode(q, kn, vn, bt, cl, max_ctx=lay.max_ctx)
     torch.cuda.synchronize()
     q_out.put((rank, float((got - ref).abs().max()), float(ref.abs().max())))
