@@ -77,6 +77,26 @@ FFI_SIGNATURES = {
 }
 
 
+ERR_NO_BLOCKS = -8
+ERR_NO_SEQ = -9
+_i32p = C.POINTER(C.c_int32)
+
+# include/clove_blocks.h: the KV block manager.
+BLOCKS_SIGNATURES = {
+    "clove_blocks_create": (_i, [_i, _i, _i, C.POINTER(_vp)]),
+    "clove_blocks_destroy": (_i, [_vp]),
+    "clove_blocks_add": (_i, [_vp, _i, _i]),
+    "clove_blocks_reserve": (_i, [_vp, _i, _i, _vp, _vp, _ip]),
+    "clove_blocks_fork": (_i, [_vp, _i, _i]),
+    "clove_blocks_free": (_i, [_vp, _i]),
+    "clove_blocks_num_free": (_i, [_vp]),
+    "clove_blocks_seq_len": (_i, [_vp, _i]),
+    "clove_blocks_seq_blocks": (_i, [_vp, _i]),
+    "clove_blocks_export": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "clove_cuda_copy_blocks": (_i, [_vp, _vp, _vp, _i, _vp]),
+}
+
+
 def load(path: Path | str = LIB_PATH) -> C.CDLL:
     path = Path(path)
     if not path.exists():
@@ -84,7 +104,7 @@ def load(path: Path | str = LIB_PATH) -> C.CDLL:
             f"{path} is missing: build it with `python -m clove_b200.build` "
             "(the CUDA extension is required; there is no fallback)")
     lib = C.CDLL(str(path))
-    for name, (res, args) in {**SIGNATURES, **FFI_SIGNATURES}.items():
+    for name, (res, args) in {**SIGNATURES, **FFI_SIGNATURES, **BLOCKS_SIGNATURES}.items():
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args

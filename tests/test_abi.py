@@ -45,6 +45,12 @@ def test_ffi_bindings_cover_header():
     assert declared == set(_lib.FFI_SIGNATURES), declared ^ set(_lib.FFI_SIGNATURES)
 
 
+def test_blocks_bindings_cover_header():
+    from clove_b200 import _lib
+    declared = _declared(ROOT / "include" / "clove_blocks.h")
+    assert declared == set(_lib.BLOCKS_SIGNATURES), declared ^ set(_lib.BLOCKS_SIGNATURES)
+
+
 def test_ffi_null_handles(lib):
     assert lib.clove_tensor_create(None, 2, 2) is None
     assert lib.clove_paged_attention(None, None, None, None, None, None) is None
