@@ -219,6 +219,8 @@ struct DecodeArgs {
   int block_size;
   const int32_t* chunk_blocks;  // device scalar: blocks per work item (set by the plan)
   int32_t* unit_counter;        // work-claim counter (zeroed by the plan)
+  const int32_t* multi;         // sequences split into several chunks (plan)
+  const int32_t* n_multi;
   int max_chunks;            // chunks per sequence, upper bound
   int max_ctx;
   int group;                 // query heads per KV head (runtime, <= template G)
@@ -245,6 +247,8 @@ struct PlanArgs {
   long long target_units;    // work units the chunk size aims for
   int32_t* chunk_blocks;     // out: blocks per work item chosen for this call
   int32_t* unit_counter;     // zeroed: the decode kernel's work-claim counter
+  int32_t* multi;            // out: sequences split into several chunks
+  int32_t* n_multi;          // out: their count
   int max_ctx;
   int append;
 };

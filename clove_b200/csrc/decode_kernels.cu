@@ -30,6 +30,7 @@
 // Semantics follow the reference's documented op: softmax(q.K^T * scale).V
 // (src/nn/attention.rs:52-69), scale 1/sqrt(head_dim) supplied by the caller
 // (src/lazy.rs:5267), block-table gather of src/lazy.rs:5259-5270.
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 #include <unordered_map>
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
     s_full = 0;
     *p.err = 0;            // flags report the most recent call only
     *p.unit_counter = 0;   // the decode kernel's work-claim counter
+    *p.n_multi = 0;
   }
   for (int i = tid; i < kPlanBins; i += kPlanThreads) hist[i] = 0;
   __syncthreads();
@@ -130,6 +132,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
       nfull = nbl / cb;
       const int rem = nbl - nfull * cb;
       p.seq_chunks[b] = nfull + (rem > 0);
+      if (nfull + (rem > 0) > 1) p.multi[atomicAdd(p.n_multi, 1)] = b;
       if (rem > 0) atomicAdd(&hist[(rem - 1) * kPlanBins / cb], 1);
       if (L == 0) {
         float* row = p.out + (size_t)b * p.row_floats;
@@ -358,23 +361,18 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
 constexpr int kCombineThreads = 128;
 constexpr int kCombineMaxChunks = 2048;  // chunk weights staged in shared memory
 
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeArgs a, int head_dim) {
-  __shared__ float w[kCombineMaxChunks];
-  __shared__ float red[kCombineThreads / 32];
-  __shared__ float s_bcast;
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+// Merge the chunks of (sequence b, query head hq): M = max m_c,
+// w_c = 2^(m_c - M), out = sum_c w_c acc_c / sum_c w_c l_c.  All threads of
+// the CTA take part; ends with a CTA barrier so the shared arrays can be
+// reused.
+__device__ void combine_one(const DecodeArgs& a, int D, int b, int hq, float* w, float* red, float* bcast) {
   const int group = a.group;
   const int Hq = a.num_kv_heads * group;
-  const int b = blockIdx.x / Hq, hq = blockIdx.x - (blockIdx.x / Hq) * Hq;
-  const int nchunks = a.seq_chunks[b];
-  if (nchunks <= 1) return;
   const int h = hq / group, g = hq - h * group;
-  const int D = head_dim;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const size_t cstride = (size_t)group * (D + 2);  // floats between consecutive chunks
   const float* base = a.partials + (((size_t)b * a.num_kv_heads + h) * a.max_chunks * group + g) * (D + 2);
-  const int nc = min(nchunks, kCombineMaxChunks);  // the plan never exceeds this (see decode_layout)
-  // 1. M = max_c m_c  (block reduction)
+  const int nc = min(a.seq_chunks[b], kCombineMaxChunks);  // decode_layout keeps it within bounds
   float mx = -INFINITY;
   for (int c = tid; c < nc; c += kCombineThreads) mx = fmaxf(mx, base[c * cstride + D]);
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -383,11 +381,10 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeAr
   if (tid == 0) {
     float m = red[0];
     for (int i = 1; i < kCombineThreads / 32; ++i) m = fmaxf(m, red[i]);
-    s_bcast = m;
+    *bcast = m;
   }
   __syncthreads();
-  const float M = s_bcast;
-  // 2. w_c = 2^(m_c - M); L = sum_c w_c l_c
+  const float M = *bcast;
   float ls = 0.f;
   for (int c = tid; c < nc; c += kCombineThreads) {
     const float wc = exp2f(base[c * cstride + D] - M);
@@ -401,11 +398,11 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeAr
   if (tid == 0) {
     float t = 0.f;
     for (int i = 0; i < kCombineThreads / 32; ++i) t += red[i];
-    s_bcast = 1.f / t;
+    *bcast = 1.f / t;
   }
   __syncthreads();
-  const float inv = s_bcast;
-  // 3. out[d] = inv * sum_c w_c acc_c[d]: loads coalesced over d, independent over c
+  const float inv = *bcast;
+  // loads coalesced over d, independent over c
   for (int d = tid; d < D; d += kCombineThreads) {
     float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
     int c = 0;
@@ -418,6 +415,21 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeAr
     for (; c < nc; ++c) o0 = fmaf(w[c], base[c * cstride + d], o0);
     a.out[((size_t)b * Hq + hq) * D + d] = ((o0 + o1) + (o2 + o3)) * inv;
   }
+  __syncthreads();
+}
+
+// Split-K combine: CTAs stride over the (sequence, query head) pairs of the
+// sequences the plan split into several chunks (the others were finished by
+// the decode kernel).  Launched as a programmatic dependent of the decode.
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeArgs a, int head_dim) {
+  __shared__ float w[kCombineMaxChunks];
+  __shared__ float red[kCombineThreads / 32];
+  __shared__ float bcast;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int Hq = a.num_kv_heads * a.group;
+  const int n_items = *a.n_multi * Hq;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x)
+    combine_one(a, head_dim, a.multi[item / Hq], item - (item / Hq) * Hq, w, red, &bcast);
 }
 
 // ---------------------------------------------------------------------------
@@ -450,6 +462,8 @@ DecodeLayout decode_layout(const clove_pool& pool, int batch, int num_q_heads, i
   L.off_items = off;
   off = align256(off + sizeof(int2) * (size_t)batch * L.max_chunks);
   L.off_seq_chunks = off;
+  off = align256(off + sizeof(int32_t) * (size_t)batch);
+  L.off_multi = off;
   off = align256(off + sizeof(int32_t) * (size_t)batch);
   L.off_partials = off;
   // Partials are only written when a sequence spans more than one chunk.
@@ -571,6 +585,8 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   p.max_chunk_blocks = (int)((2u << 20) / (2u * pool.block_size * pool.head_dim * pool.elem_bytes));
   p.chunk_blocks = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 1;
   p.unit_counter = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 2;
+  p.n_multi = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 3;
+  p.multi = reinterpret_cast<int32_t*>(ws + L.off_multi);
   p.max_ctx = call.max_ctx;
   p.append = append;
   plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
@@ -602,6 +618,8 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   a.block_size = pool.block_size;
   a.chunk_blocks = p.chunk_blocks;
   a.unit_counter = p.unit_counter;
+  a.multi = p.multi;
+  a.n_multi = p.n_multi;
   a.max_chunks = L.max_chunks;
   a.max_ctx = call.max_ctx;
   a.group = call.num_q_heads / pool.num_kv_heads;
@@ -623,7 +641,8 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   // Split-K combine for the sequences the plan split into several chunks.
   {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(call.batch * call.num_q_heads));
+    cfg.gridDim = dim3((unsigned)std::min<long long>((long long)call.batch * call.num_q_heads,
+                                                     (long long)pool.num_sms * 8));
     cfg.blockDim = dim3(kCombineThreads);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

@@ -39,7 +39,7 @@ namespace clove {
 struct DecodeLayout {
   int chunk_blocks;  // the smallest chunk the plan may choose
   int max_chunks;    // chunks per sequence at that size (workspace bound)
-  size_t off_err, off_nitems, off_items, off_seq_chunks, off_partials;
+  size_t off_err, off_nitems, off_items, off_seq_chunks, off_multi, off_partials;
   size_t total;
 };
 
