@@ -29,9 +29,9 @@ METRIC = "paged-attn decode tokens/s"
 
 # DRAM bytes (read + write) per decode launch on rank 0's default workload,
 # from the ncu captures summarised in profiles/ (paged_decode_simt_c2.md,
-# paged_decode_mma_c3_c5.md).  Reported as roofline.traffic next to the
+# paged_decode_mma_c3_c4.md).  Reported as roofline.traffic next to the
 # algorithmic bytes; None where no full-size capture exists.
-TRAFFIC_MEASURED = {"c2": 4338.4e6, "c3": 694.1e6}
+TRAFFIC_MEASURED = {"c2": 4334.7e6, "c3": 694.3e6}
 
 
 def _peaks() -> tuple[float, str]:
