@@ -92,5 +92,20 @@ class PagedAttention:
         attn = CudaBackend.paged_attention(q, k, v, kv_cache, block_tables, context_lens, max_ctx=max_ctx)
         return self.w_o.forward(attn)
 
+    def prefill(self, x: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
+                context_lens: torch.Tensor, cu_seqlens: torch.Tensor, max_ctx: int,
+                rope_theta: float = 0.0) -> torch.Tensor:
+        """Prompt pass: x [num_tokens, dim] packed by cu_seqlens; writes the
+        prompt's K/V into the paged cache and returns [num_tokens, dim].  The
+        attention is the reference's causal FlashAttention step
+        (src/lazy.rs:4821-4923) on the paged cache (CudaBackend path)."""
+        pool = CudaBackend._pool(kv_cache)
+        T = x.shape[0]
+        q = self.w_q.forward(x).reshape(T, self.num_heads, self.head_dim).contiguous()
+        k = self.w_k.forward(x).reshape(T, self.num_kv_heads, self.head_dim).contiguous()
+        v = self.w_v.forward(x).reshape(T, self.num_kv_heads, self.head_dim).contiguous()
+        attn = pool.prefill(q, k, v, cu_seqlens, block_tables, context_lens, max_ctx=max_ctx, rope_theta=rope_theta)
+        return self.w_o.forward(attn.reshape(T, -1))
+
     def parameters(self) -> list[torch.Tensor]:
         return [t for l in (self.w_q, self.w_k, self.w_v, self.w_o) for t in (l.weight, l.bias)]

@@ -1,0 +1,211 @@
+// Prefill into the paged cache: the prompt tokens of each sequence are
+// (optionally) rotated with RoPE, written to their cache slots, and attend
+// causally over the sequence's cache — prior context plus the prompt up to
+// themselves.
+//
+// The attention reuses the decode pipeline: every new token is a query row
+// whose context is the sequence's cache up to and including its own
+// position.  A prep kernel writes the rotated K/V into the slots, the rotated
+// queries into the workspace, and expands one block-table row and context
+// length per token; the decode kernels (plan -> decode -> combine) then run
+// over those rows.  The rows of one sequence read the same K/V tiles, which
+// the 126 MB L2 serves for all but the longest prompts.
+//
+// Semantics follow the reference's FlashAttention step (src/lazy.rs:4821-4923:
+// causal mask, RoPE on q and k, scale 1/sqrt(head_dim)) with the exact
+// exponential in place of its polynomial approximation (lazy.rs:4846-4851).
+#include <cmath>
+
+#include "../../include/clove_cuda.h"
+#include "common.cuh"
+#include "host.h"
+
+namespace clove {
+
+struct PrefillPrepArgs {
+  const void* q;   // [T, Hq, D]
+  const void* k;   // [T, Hkv, D]
+  const void* v;
+  const int32_t* cu_seqlens;    // [B + 1]
+  const int32_t* block_tables;  // [B, bt_stride]
+  const int32_t* context_lens;  // [B] cached tokens before the prompt
+  void* k_cache;
+  void* v_cache;
+  void* q_rot;            // out [T, Hq, D]
+  int32_t* row_tables;    // out [T, bt_stride]
+  int32_t* row_lens;      // out [T] = position + 1
+  int32_t* flags;
+  int batch, num_tokens, hq, hkv, D, bs, bt_stride, num_blocks, max_ctx;
+  float rope_theta;       // 0: no rotation
+};
+
+template <typename T>
+__device__ __forceinline__ T from_f(float x);
+template <> __device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
+
+// Rotate one head row in place semantics: out[2i], out[2i+1] from in[2i],
+// in[2i+1] by angle pos * theta^(-2i/D) (pairs of adjacent elements, the
+// pairing of src/lazy.rs:4834-4842).
+template <typename T>
+__device__ void rope_row(const T* in, T* out, int D, int pos, float theta, int lane0, int stride) {
+  for (int i = lane0; i < D / 2; i += stride) {
+    const float x0 = Elem<T>::to_f(in[2 * i]), x1 = Elem<T>::to_f(in[2 * i + 1]);
+    if (theta > 0.f) {
+      const float ang = (float)pos * powf(theta, -2.f * (float)i / (float)D);
+      float sn, cs;
+      sincosf(ang, &sn, &cs);
+      out[2 * i] = from_f<T>(x0 * cs - x1 * sn);
+      out[2 * i + 1] = from_f<T>(x0 * sn + x1 * cs);
+    } else {
+      out[2 * i] = in[2 * i];
+      out[2 * i + 1] = in[2 * i + 1];
+    }
+  }
+}
+
+// One CTA per prompt token.
+template <typename T>
+__global__ void __launch_bounds__(128) prefill_prep_kernel(const PrefillPrepArgs p) {
+  const int t = blockIdx.x;
+  // sequence of token t: largest b with cu_seqlens[b] <= t
+  int lo = 0, hi = p.batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(p.cu_seqlens + mid) <= t) lo = mid; else hi = mid - 1;
+  }
+  const int b = lo;
+  const int pos = __ldg(p.context_lens + b) + (t - __ldg(p.cu_seqlens + b));
+  const int32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
+  const bool in_range = pos >= 0 && pos < p.max_ctx && pos / p.bs < p.bt_stride;
+  // expanded table row and length
+  for (int j = threadIdx.x; j < p.bt_stride; j += blockDim.x) p.row_tables[(size_t)t * p.bt_stride + j] = bt[j];
+  if (threadIdx.x == 0) {
+    p.row_lens[t] = in_range ? pos + 1 : 0;
+    if (!in_range) atomicOr(p.flags, CLOVE_FLAG_CTX_RANGE);
+  }
+  // rotated query rows
+  const T* qs = static_cast<const T*>(p.q) + (size_t)t * p.hq * p.D;
+  T* qd = static_cast<T*>(p.q_rot) + (size_t)t * p.hq * p.D;
+  for (int h = 0; h < p.hq; ++h) rope_row<T>(qs + h * p.D, qd + h * p.D, p.D, pos, p.rope_theta, threadIdx.x, blockDim.x);
+  if (!in_range) return;
+  // K (rotated) and V into the slot
+  const int phys = __ldg(bt + pos / p.bs);
+  if (phys < 0 || phys >= p.num_blocks) {
+    if (threadIdx.x == 0) atomicOr(p.flags, CLOVE_FLAG_BLOCK_OOB);
+    return;
+  }
+  const size_t row = ((size_t)phys * p.bs + pos % p.bs) * p.hkv * p.D;
+  const T* ks = static_cast<const T*>(p.k) + (size_t)t * p.hkv * p.D;
+  const T* vs = static_cast<const T*>(p.v) + (size_t)t * p.hkv * p.D;
+  T* kc = static_cast<T*>(p.k_cache) + row;
+  T* vc = static_cast<T*>(p.v_cache) + row;
+  for (int h = 0; h < p.hkv; ++h) rope_row<T>(ks + h * p.D, kc + h * p.D, p.D, pos, p.rope_theta, threadIdx.x, blockDim.x);
+  for (int i = threadIdx.x; i < p.hkv * p.D; i += blockDim.x) vc[i] = vs[i];
+}
+
+struct PrefillLayout {
+  size_t off_q, off_tables, off_lens, off_decode, total;
+};
+
+static size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static PrefillLayout prefill_layout(const clove_pool& pool, int num_tokens, int num_q_heads, int bt_stride,
+                                    int max_ctx) {
+  PrefillLayout L;
+  size_t off = 0;
+  L.off_q = off;
+  off = al256(off + (size_t)num_tokens * num_q_heads * pool.head_dim * pool.elem_bytes);
+  L.off_tables = off;
+  off = al256(off + (size_t)num_tokens * bt_stride * 4);
+  L.off_lens = off;
+  off = al256(off + (size_t)num_tokens * 4);
+  L.off_decode = off;
+  off += decode_layout(pool, num_tokens, num_q_heads, max_ctx).total;
+  L.total = off;
+  return L;
+}
+
+}  // namespace clove
+
+using namespace clove;
+
+extern "C" {
+
+size_t clove_cuda_prefill_workspace_size(clove_pool_t pool, int num_tokens, int num_q_heads, int bt_stride,
+                                         int max_ctx) {
+  if (!pool || num_tokens <= 0 || num_q_heads <= 0 || bt_stride <= 0 || max_ctx <= 0) return 0;
+  return prefill_layout(*pool, num_tokens, num_q_heads, bt_stride, max_ctx).total;
+}
+
+int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, const void* v,
+                             const int32_t* cu_seqlens, const int32_t* block_tables, int bt_stride,
+                             const int32_t* context_lens, int batch, int num_tokens, int num_q_heads, float scale,
+                             float rope_theta, int max_ctx, float* out, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  if (!pool || batch <= 0 || num_tokens < 0 || num_q_heads <= 0 || bt_stride <= 0 || max_ctx <= 0 ||
+      rope_theta < 0.f) {
+    set_last_error("paged_prefill: bad arguments");
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  if (num_tokens == 0) return CLOVE_OK;
+  if (!q || !k || !v || !cu_seqlens || !block_tables || !context_lens || !out || !workspace ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u)) {
+    set_last_error("paged_prefill: null pointer or workspace not 256-byte aligned");
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  if (num_q_heads % pool->num_kv_heads || (long long)max_ctx > (long long)bt_stride * pool->block_size) {
+    set_last_error("paged_prefill: num_q_heads / max_ctx inconsistent with the pool and tables");
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  const PrefillLayout L = prefill_layout(*pool, num_tokens, num_q_heads, bt_stride, max_ctx);
+  if (workspace_bytes < L.total) {
+    set_last_error("paged_prefill: workspace %zu bytes < required %zu", workspace_bytes, L.total);
+    return CLOVE_ERR_WORKSPACE;
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != pool->device) cudaSetDevice(pool->device);
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  PrefillPrepArgs p;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.cu_seqlens = cu_seqlens;
+  p.block_tables = block_tables;
+  p.context_lens = context_lens;
+  p.k_cache = pool->k_cache;
+  p.v_cache = pool->v_cache;
+  p.q_rot = ws + L.off_q;
+  p.row_tables = reinterpret_cast<int32_t*>(ws + L.off_tables);
+  p.row_lens = reinterpret_cast<int32_t*>(ws + L.off_lens);
+  p.flags = pool->flags;
+  p.batch = batch;
+  p.num_tokens = num_tokens;
+  p.hq = num_q_heads;
+  p.hkv = pool->num_kv_heads;
+  p.D = pool->head_dim;
+  p.bs = pool->block_size;
+  p.bt_stride = bt_stride;
+  p.num_blocks = pool->num_blocks;
+  p.max_ctx = max_ctx;
+  p.rope_theta = rope_theta;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (pool->dtype) {
+    case CLOVE_DTYPE_F32: prefill_prep_kernel<float><<<num_tokens, 128, 0, s>>>(p); break;
+    case CLOVE_DTYPE_BF16: prefill_prep_kernel<__nv_bfloat16><<<num_tokens, 128, 0, s>>>(p); break;
+    default: prefill_prep_kernel<__half><<<num_tokens, 128, 0, s>>>(p); break;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (prev >= 0 && prev != pool->device) cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    set_last_error("paged_prefill prep launch: %s", cudaGetErrorString(e));
+    return CLOVE_ERR_CUDA;
+  }
+  count_launches(1);
+  return clove_cuda_paged_decode(pool, ws + L.off_q, num_q_heads, p.row_tables, bt_stride, p.row_lens, num_tokens,
+                                 scale, max_ctx, out, ws + L.off_decode, L.total - L.off_decode, stream);
+}
+
+}  // extern "C"

@@ -178,6 +178,31 @@ class KVPool:
     def append_decode(self, q, k_new, v_new, block_tables, context_lens, **kw) -> torch.Tensor:
         return self.decode(q, block_tables, context_lens, k_new=k_new, v_new=v_new, **kw)
 
+    def prefill(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
+                block_tables: torch.Tensor, context_lens: torch.Tensor, max_ctx: int, scale: float | None = None,
+                rope_theta: float = 0.0, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """Prefill packed prompts: write their K/V (RoPE-rotated K when
+        rope_theta > 0) into the cache and return each token's causal
+        attention output, f32 [num_tokens, num_q_heads, head_dim]."""
+        T = q.shape[0]
+        hq = q.shape[1] if q.dim() == 3 else q.shape[1] // self.head_dim
+        q = self._check_rows(q, T, hq, "q")
+        k = self._check_rows(k, T, self.num_kv_heads, "k")
+        v = self._check_rows(v, T, self.num_kv_heads, "v")
+        for t, n in ((cu_seqlens, "cu_seqlens"), (block_tables, "block_tables"), (context_lens, "context_lens")):
+            self._check_i32(t, n)
+        batch = context_lens.numel()
+        if scale is None:
+            scale = 1.0 / math.sqrt(self.head_dim)
+        out = torch.empty((T, hq, self.head_dim), dtype=torch.float32, device=self.device)
+        n = int(self._lib.clove_cuda_prefill_workspace_size(self.handle, T, hq, block_tables.shape[1], max_ctx))
+        ws = torch.empty(max(n, 256), dtype=torch.uint8, device=self.device)
+        _lib.check(self._lib.clove_cuda_paged_prefill(
+            self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(cu_seqlens), _ptr(block_tables), block_tables.shape[1],
+            _ptr(context_lens), batch, T, hq, float(scale), float(rope_theta), max_ctx, _ptr(out), _ptr(ws),
+            ws.numel(), _stream(stream)))
+        return out
+
     def decode_status(self, batch: int, num_q_heads: int, max_ctx: int,
                       stream: torch.cuda.Stream | None = None) -> int:
         """Device check flags of the most recent decode on that workspace."""

@@ -164,6 +164,31 @@ int clove_cuda_paged_append_decode(clove_pool_t pool, const void* q,
                                    void* workspace, size_t workspace_bytes,
                                    void* stream);
 
+/* Prefill into the paged cache (the step before decode; the reference's
+ * FlashAttention step, src/lazy.rs:4821-4923, causal, RoPE on q and k, scale
+ * 1/sqrt(head_dim)).  The prompt tokens of `batch` sequences are packed:
+ * q [num_tokens, num_q_heads, D], k, v [num_tokens, num_kv_heads, D] in the
+ * pool dtype; sequence b owns tokens cu_seqlens[b] .. cu_seqlens[b+1]-1 (int32
+ * [batch+1], device) at positions context_lens[b] + i (context_lens: cached
+ * tokens before the prompt; 0 for a fresh prompt).  With rope_theta > 0, q
+ * and k are rotated in adjacent pairs (2i, 2i+1) by pos * theta^(-2i/D)
+ * (theta 10000 in the reference); 0 disables RoPE.  K and V (rotated K) are
+ * written to their slots through block_tables; out f32 [num_tokens,
+ * num_q_heads, D] is each token's causal attention over its sequence's cache
+ * up to and including itself.  max_ctx bounds context_lens[b] + prompt
+ * length.  Scratch: clove_cuda_prefill_workspace_size bytes. */
+size_t clove_cuda_prefill_workspace_size(clove_pool_t pool, int num_tokens,
+                                         int num_q_heads, int bt_stride,
+                                         int max_ctx);
+int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k,
+                             const void* v, const int32_t* cu_seqlens,
+                             const int32_t* block_tables, int bt_stride,
+                             const int32_t* context_lens, int batch,
+                             int num_tokens, int num_q_heads, float scale,
+                             float rope_theta, int max_ctx, float* out,
+                             void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* Append + decode for callers that cannot allocate device memory when they
  * decode (an engine that hands all of HBM to its KV pool at start-up, a host
  * whose device memory comes only from an allocator it may not call on the

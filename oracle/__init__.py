@@ -148,3 +148,20 @@ def tolerance_ok(x: np.ndarray, ref: np.ndarray, rtol: float) -> tuple[bool, flo
     ratio = np.abs(x - r) / bound
     worst = float(ratio.max()) * rtol if ratio.size else 0.0
     return bool((ratio <= 1.0).all()), worst
+
+
+def rope(x: np.ndarray, positions, theta: float) -> np.ndarray:
+    """float64 rotation of [..., tokens, heads, D] rows in adjacent pairs
+    (2i, 2i+1) by pos * theta^(-2i/D) — apply_rope of the reference's
+    FlashAttention shader (src/lazy.rs:4834-4842: angle = pos /
+    10000^(i/head_dim) for the even index i).  positions: [tokens]."""
+    x = np.asarray(x, np.float64)
+    D = x.shape[-1]
+    i = np.arange(D // 2)
+    ang = np.asarray(positions, np.float64)[:, None] * theta ** (-2.0 * i / D)  # [T, D/2]
+    c, s = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    out = np.empty_like(x)
+    out[..., 0::2] = x0 * c - x1 * s
+    out[..., 1::2] = x0 * s + x1 * c
+    return out
