@@ -61,6 +61,7 @@ SIGNATURES = {
     "clove_cuda_decode_status": (_i, [_vp, _vp, _ip]),
     "clove_cuda_set_decode_variant": (_i, [_i]),
     "clove_cuda_launch_count": (C.c_uint64, []),
+    "clove_cuda_debug_set": (_i, [C.c_uint32, _i]),
 }
 
 

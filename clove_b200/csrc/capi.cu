@@ -16,6 +16,8 @@ namespace clove {
 static thread_local char g_last_error[512] = {0};
 static std::atomic<uint64_t> g_launches{0};
 static std::atomic<int> g_variant{0};
+static std::atomic<uint32_t> g_wait_limit{1u << 24};
+static std::atomic<int> g_inject_stall{0};
 
 void set_last_error(const char* fmt, ...) {
   va_list ap;
@@ -26,6 +28,8 @@ void set_last_error(const char* fmt, ...) {
 
 void count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 int decode_variant() { return g_variant.load(std::memory_order_relaxed); }
+uint32_t debug_wait_limit() { return g_wait_limit.load(std::memory_order_relaxed); }
+int debug_inject_stall() { return g_inject_stall.load(std::memory_order_relaxed); }
 
 static int cuda_fail(const char* what, cudaError_t e) {
   set_last_error("%s: %s", what, cudaGetErrorString(e));
@@ -496,5 +500,11 @@ int clove_cuda_set_decode_variant(int variant) {
 }
 
 uint64_t clove_cuda_launch_count(void) { return g_launches.load(); }
+
+int clove_cuda_debug_set(uint32_t wait_limit, int inject_stall) {
+  g_wait_limit.store(wait_limit ? wait_limit : (1u << 24));
+  g_inject_stall.store(inject_stall ? 1 : 0);
+  return CLOVE_OK;
+}
 
 }  // extern "C"

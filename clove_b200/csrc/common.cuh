@@ -117,8 +117,9 @@ constexpr uint32_t kWaitLimit = 1u << 24;
 
 // Bounded wait on `bar` completing the phase with `parity`.  Returns false
 // (and sets CLOVE_FLAG_TIMEOUT in *err) if the limit ran out.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
+                                                  uint32_t limit = kWaitLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
   }
   atomicOr(err, CLOVE_FLAG_TIMEOUT);
@@ -228,6 +229,8 @@ struct DecodeArgs {
   int nstage;                // pipeline depth (a multiple of ncw)
   int ncw;                   // consumer warps that take stages (<= the kernel's NCW)
   int stage_blocks;          // blocks per pipeline stage (1..4)
+  uint32_t wait_limit;       // polls before a pipeline wait is declared stuck
+  int inject_stall;          // test hook: the first stage of unit 0 is never filled
   float qscale;              // scale * log2(e)
 };
 

@@ -229,7 +229,7 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
     // ---- post the unit (or the end marker) to the unit ring ----
     int ok = 1;
     if (lane == 0) {
-      if (*sm.misc || !mbar_wait_bounded(&sm.uempty[uk], uphase ^ 1, a.err)) {
+      if (*sm.misc || !mbar_wait_bounded(&sm.uempty[uk], uphase ^ 1, a.err, a.wait_limit)) {
         ok = 0;
         *sm.misc = 1;
       } else if (u >= n_units) {
@@ -269,9 +269,12 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
       for (int i = 0; i < 4; ++i) phys[i] = __shfl_sync(0xffffffffu, my, (j0 + i) & 31);
       ok = 1;
       if (lane == 0) {
-        if (*sm.misc || !mbar_wait_bounded(&sm.empty[slot], phase ^ 1, a.err)) {
+        if (*sm.misc || !mbar_wait_bounded(&sm.empty[slot], phase ^ 1, a.err, a.wait_limit)) {
           ok = 0;
           *sm.misc = 1;
+        } else if (a.inject_stall && u == 0 && s == 0) {
+          // test hook: the first stage of the first unit is never filled, so
+          // its consumer's wait runs out
         } else {
           mbar_arrive_expect_tx(&sm.full[slot], 2u * tile_bytes * (uint32_t)nb);
           unsigned char* st = sm.ring + (size_t)slot * sp.stage_bytes;
@@ -311,7 +314,7 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
         s = a.nstage - 1;
         ph ^= 1;
       }
-      for (uint32_t i = 0; i < kWaitLimit; ++i)
+      for (uint32_t i = 0; i < a.wait_limit; ++i)
         if (mbar_try_wait(&sm.full[s], ph)) break;
     }
     int k2 = uk;
@@ -321,7 +324,7 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
         k2 = kUnitRing - 1;
         uph ^= 1;
       }
-      for (uint32_t i = 0; i < kWaitLimit; ++i)
+      for (uint32_t i = 0; i < a.wait_limit; ++i)
         if (mbar_try_wait(&sm.ufull[k2], uph)) break;
     }
   }
@@ -333,7 +336,7 @@ __device__ void produce(const DecodeArgs& a, const CUtensorMap* tm_k, const CUte
 // wait, so no warp is ever left at a barrier).
 __device__ __forceinline__ bool wait_unit(const DecodeArgs& a, const SmemPtrs& sm, int uk, uint32_t uphase,
                                           UnitSlot& out) {
-  if (sm.misc[0] || !mbar_wait_bounded(&sm.ufull[uk], uphase, a.err)) {
+  if (sm.misc[0] || !mbar_wait_bounded(&sm.ufull[uk], uphase, a.err, a.wait_limit)) {
     sm.misc[0] = 1;
     return false;
   }
@@ -343,7 +346,7 @@ __device__ __forceinline__ bool wait_unit(const DecodeArgs& a, const SmemPtrs& s
 
 __device__ __forceinline__ bool wait_or_abort(const DecodeArgs& a, const SmemPtrs& sm, uint64_t* bar,
                                               uint32_t parity) {
-  if (sm.misc[0] || !mbar_wait_bounded(bar, parity, a.err)) {
+  if (sm.misc[0] || !mbar_wait_bounded(bar, parity, a.err, a.wait_limit)) {
     sm.misc[0] = 1;
     return false;
   }

@@ -255,7 +255,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       const int gs = gbase + j;
       const int slot = gs % a.nstage;
       const uint32_t par = (uint32_t)(gs / a.nstage) & 1u;
-      if (sm.misc[0] || !mbar_wait_bounded(&sm.full[slot], par, a.err)) {
+      if (sm.misc[0] || !mbar_wait_bounded(&sm.full[slot], par, a.err, a.wait_limit)) {
         sm.misc[0] = 1;
         aborted = true;
         break;
@@ -626,6 +626,8 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   a.append = append;
   a.nstage = 2;
   a.ncw = 1;
+  a.wait_limit = debug_wait_limit();
+  a.inject_stall = debug_inject_stall();
   a.qscale = call.scale * kLog2e;
 
   int rc;

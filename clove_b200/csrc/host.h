@@ -95,5 +95,7 @@ cudaError_t launch_dependent(Kern kern, unsigned grid, unsigned threads, size_t 
 void set_last_error(const char* fmt, ...);
 void count_launches(int n);
 int decode_variant();  // 0 auto, 1 simt, 2 mma
+uint32_t debug_wait_limit();
+int debug_inject_stall();
 
 }  // namespace clove

@@ -161,7 +161,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       const int gs = gbase + j;
       const int slot = gs % a.nstage;
       const uint32_t par = (uint32_t)(gs / a.nstage) & 1u;
-      if (sm.misc[0] || !mbar_wait_bounded(&sm.full[slot], par, a.err)) {
+      if (sm.misc[0] || !mbar_wait_bounded(&sm.full[slot], par, a.err, a.wait_limit)) {
         sm.misc[0] = 1;
         aborted = true;
         break;

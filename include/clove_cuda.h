@@ -224,6 +224,14 @@ int clove_cuda_set_decode_variant(int variant);
  * launch count). */
 uint64_t clove_cuda_launch_count(void);
 
+/* Testing hook (failure detection without a GPU fault).  wait_limit: polls
+ * after which a pipeline wait gives up (0 = the default, seconds of wall
+ * time); inject_stall = 1 makes one CTA's producer skip one stage's copy, so
+ * its consumer's bounded wait runs out: the call then completes, reports
+ * CLOVE_FLAG_TIMEOUT through clove_cuda_decode_status, and its output is
+ * undefined.  Process-wide; never set it in production. */
+int clove_cuda_debug_set(uint32_t wait_limit, int inject_stall);
+
 #ifdef __cplusplus
 }
 #endif

@@ -138,3 +138,39 @@ def test_workspace_writes_stay_in_bounds(variant, group):
         set_decode_variant("auto")
     assert (buf[need:] == 0xAB).all(), "decode wrote past the workspace size it reported"
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("variant,dtype,group", [("mma", torch.bfloat16, 4), ("simt", torch.float32, 1)])
+def test_stuck_pipeline_wait_times_out_and_context_survives(variant, dtype, group):
+    # Failure detection without a GPU fault: one stage is never filled (test
+    # hook), so its consumer's bounded wait runs out; the call must finish,
+    # report CLOVE_FLAG_TIMEOUT, and the next call must work normally.
+    import time
+
+    from clove_b200 import set_decode_variant
+    from clove_b200.workload import Spec, make_layout
+    from workload_check import run_layout_vs_oracle
+    L = _lib.lib()
+    spec = Spec("t", 8, 2 * group, 2, 128, 16, 0, dtype, "uniform", 200, 900, "permutation", seed=19)
+    lay = make_layout(spec)
+    from clove_b200 import KVPool
+    from clove_b200.workload import fill_values
+    dev = torch.device("cuda", 0)
+    pool = KVPool(lay.num_blocks, 16, 2, 128, dtype, 0)
+    q, kn, vn, _ = fill_values(lay, dev, pool.storage)
+    bt = torch.from_numpy(lay.block_tables).to(dev)
+    cl = torch.from_numpy(lay.context_lens).to(dev)
+    set_decode_variant(variant)
+    try:
+        _lib.check(L.clove_cuda_debug_set(2000, 1))
+        t0 = time.time()
+        pool.append_decode(q, kn, vn, bt, cl, max_ctx=lay.max_ctx)
+        flags = pool.decode_status(lay.batch, spec.num_q_heads, lay.max_ctx)
+        elapsed = time.time() - t0
+    finally:
+        L.clove_cuda_debug_set(0, 0)
+        set_decode_variant("auto")
+    assert flags & _lib.FLAG_TIMEOUT, flags
+    assert elapsed < 30
+    # the context is intact: a normal call on a fresh workload is correct
+    run_layout_vs_oracle(make_layout(spec, seed=23), 1e-5 if dtype == torch.float32 else 2e-2)

@@ -77,3 +77,23 @@ def test_two_rank_sharding_matches_unsharded(mode, oracle_lib):
                                 1.0 / np.sqrt(lay.spec.head_dim))
     for r in range(2):
         np.testing.assert_array_equal(results[r], ref)
+
+
+def _lonely_worker(port, q_out):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE="2", RANK="0", LOCAL_RANK="0")
+    try:
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=5))
+        q_out.put("joined")
+    except Exception as e:  # the peer never joins: a bounded error, not a hang
+        q_out.put("error:" + type(e).__name__)
+
+
+def test_rank_that_never_joins_gives_a_timeout_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_lonely_worker, args=(_free_port(), q))
+    p.start()
+    res = q.get(timeout=120)
+    p.join(timeout=60)
+    assert res.startswith("error:"), res
