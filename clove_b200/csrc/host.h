@@ -75,9 +75,9 @@ cudaError_t launch_gather_kv(const void* k_cache, const void* v_cache, const int
 // Launch a decode kernel as a programmatic dependent of the previous kernel
 // on the stream (the plan): it may start early and must execute
 // griddepcontrol.wait before reading the plan's outputs.
-template <typename Kern>
+template <typename Kern, typename Args>
 cudaError_t launch_dependent(Kern kern, unsigned grid, unsigned threads, size_t smem, cudaStream_t stream,
-                             const CUtensorMap& tk, const CUtensorMap& tv, const DecodeArgs& a) {
+                             const CUtensorMap& tk, const CUtensorMap& tv, const Args& a) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(threads);
@@ -90,6 +90,10 @@ cudaError_t launch_dependent(Kern kern, unsigned grid, unsigned threads, size_t 
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, tk, tv, a);
 }
+
+int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
+                       const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
+                       int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);
 
 // error text / launch accounting (capi.cu)
 void set_last_error(const char* fmt, ...);

@@ -22,63 +22,10 @@
 #include "common.cuh"
 #include "decode_common.cuh"
 #include "host.h"
+#include "mma_common.cuh"
 #include "mma_decode.cuh"
 
 namespace clove {
-
-template <typename T> struct MmaType;
-template <> struct MmaType<__nv_bfloat16> {
-  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-  }
-};
-template <> struct MmaType<__half> {
-  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
-    __half2 v = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-  }
-};
-
-// D(16x8, f32) += A(16x16) * B(16x8) with A rows 8..15 zero (registers a1,
-// a3 = 0): only d0, d1 (row lane/4) carry results, so the accumulator is the
-// pair (d0, d1); the zero rows are fed in as constants and their outputs
-// discarded.
-template <typename T>
-__device__ __forceinline__ void mma16816(float (&d)[2], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  const uint32_t z = 0;
-  const float zf = 0.f;
-  float x2, x3;
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(x2), "=f"(x3)
-        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1), "f"(d[0]), "f"(d[1]), "f"(zf), "f"(zf));
-  } else {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(x2), "=f"(x3)
-        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1), "f"(d[0]), "f"(d[1]), "f"(zf), "f"(zf));
-  }
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // Byte offset, inside a stage's K (or V) region, of 16-byte chunk `ch`
 // (head_dim / 8 chunks per token) of token `tok` (0 .. sb*block_size-1).

@@ -204,6 +204,18 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, co
     return CLOVE_ERR_CUDA;
   }
   count_launches(1);
+  // Tensor-core prefill kernel where the shape is covered (16-bit pools,
+  // head_dim 64/128, group <= 16), unless the CUDA-core variant is forced;
+  // otherwise every prompt token runs as a decode query row over the cache.
+  if (decode_variant() != 1) {
+    int prev2 = -1;
+    cudaGetDevice(&prev2);
+    if (prev2 != pool->device) cudaSetDevice(pool->device);
+    const int rc = launch_prefill_mma(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride,
+                                      batch, num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);
+    if (prev2 >= 0 && prev2 != pool->device) cudaSetDevice(prev2);
+    if (rc != CLOVE_ERR_UNSUPPORTED) return rc;
+  }
   return clove_cuda_paged_decode(pool, ws + L.off_q, num_q_heads, p.row_tables, bt_stride, p.row_lens, num_tokens,
                                  scale, max_ctx, out, ws + L.off_decode, L.total - L.off_decode, stream);
 }

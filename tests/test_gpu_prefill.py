@@ -43,18 +43,29 @@ def _case(dtype, hq, hkv, d, bs, prior, prompt, seed):
     (torch.float32, 8, 2, 128, 16, 10000.0),
     (torch.bfloat16, 8, 2, 128, 32, 10000.0),
     (torch.float16, 16, 2, 64, 8, 500.0),
+    (torch.bfloat16, 24, 8, 128, 16, 10000.0),
+    (torch.bfloat16, 32, 2, 64, 16, 0.0),
+    (torch.float16, 6, 2, 128, 64, 10000.0),
 ])
-def test_prefill_matches_oracle(dtype, hq, hkv, d, bs, theta):
+@pytest.mark.parametrize("variant", ["auto", "simt"])
+def test_prefill_matches_oracle(dtype, hq, hkv, d, bs, theta, variant):
     import oracle
-    from clove_b200 import KVPool
+    from clove_b200 import KVPool, set_decode_variant
+    if variant == "simt" and hq // hkv > 8:
+        pytest.skip("the decode-reuse prefill covers groups <= 8 (the tensor-core path covers up to 16)")
     c = _case(dtype, hq, hkv, d, bs, prior=[0, 21, 0, 40], prompt=[17, 9, 1, 33], seed=hq + bs)
     pool = KVPool(c["nb"], bs, hkv, d, dtype, 0)
     pool.storage.normal_()
     before = to_numpy_bits(pool.storage)
     dev = torch.device("cuda", 0)
-    out = pool.prefill(c["q"], c["k"], c["v"], torch.from_numpy(c["cu"]).to(dev), torch.from_numpy(c["bt"]).to(dev),
-                       torch.from_numpy(c["ctx"]).to(dev), max_ctx=int(c["total"].max()), rope_theta=theta)
-    torch.cuda.synchronize()
+    set_decode_variant(variant)
+    try:
+        out = pool.prefill(c["q"], c["k"], c["v"], torch.from_numpy(c["cu"]).to(dev),
+                           torch.from_numpy(c["bt"]).to(dev), torch.from_numpy(c["ctx"]).to(dev),
+                           max_ctx=int(c["total"].max()), rope_theta=theta)
+        torch.cuda.synchronize()
+    finally:
+        set_decode_variant("auto")
     assert pool.pool_status() == 0
     after = to_numpy_bits(pool.storage)
     # host reference: positions, (rotated) K written into the slots, V as is
