@@ -69,7 +69,7 @@ class KVPool:
             self.device.index, storage[0].data_ptr(), storage[1].data_ptr(), num_blocks, block_size,
             num_kv_heads, head_dim, _DTYPES[dtype], C.byref(h)))
         self.handle = h
-        self._ws: dict[tuple[int, int, int], torch.Tensor] = {}
+        self._ws: torch.Tensor | None = None
 
     @property
     def k_cache(self) -> torch.Tensor:
@@ -95,13 +95,15 @@ class KVPool:
         return int(self._lib.clove_cuda_decode_workspace_size(self.handle, batch, num_q_heads, max_ctx))
 
     def workspace(self, batch: int, num_q_heads: int, max_ctx: int) -> torch.Tensor:
-        key = (batch, num_q_heads, max_ctx)
-        ws = self._ws.get(key)
-        if ws is None:
-            n = self.workspace_bytes(batch, num_q_heads, max_ctx)
-            ws = torch.zeros(max(n, 256), dtype=torch.uint8, device=self.device)
-            self._ws[key] = ws
-        return ws
+        """The pool's decode scratch, grown (never shrunk) to fit this call.
+        Calls on one stream may share it; the check-flag word lives at its
+        start, so decode_status reads the most recent call's flags."""
+        n = max(self.workspace_bytes(batch, num_q_heads, max_ctx), 256)
+        if self._ws is None or self._ws.numel() < n:
+            if self._ws is not None:
+                torch.cuda.current_stream(self.device).synchronize()  # queued calls may still use the old one
+            self._ws = torch.zeros(n, dtype=torch.uint8, device=self.device)
+        return self._ws
 
     # ---- ops ---------------------------------------------------------------
     def _check_rows(self, t: torch.Tensor, rows: int, heads: int, name: str) -> torch.Tensor:
@@ -205,8 +207,11 @@ class KVPool:
 
     def decode_status(self, batch: int, num_q_heads: int, max_ctx: int,
                       stream: torch.cuda.Stream | None = None) -> int:
-        """Device check flags of the most recent decode on that workspace."""
-        ws = self.workspace(batch, num_q_heads, max_ctx)
+        """Device check flags of the most recent decode (the arguments are
+        kept for the interface; every decode of the pool shares one workspace)."""
+        if self._ws is None:
+            return 0
+        ws = self._ws
         flags = C.c_int(0)
         rc = self._lib.clove_cuda_decode_status(_ptr(ws), _stream(stream), C.byref(flags))
         if rc not in (_lib.OK, _lib.ERR_DEVICE_CHECK):
