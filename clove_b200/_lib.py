@@ -58,6 +58,10 @@ SIGNATURES = {
     "clove_cuda_prefill_workspace_size": (_sz, [_vp, _i, _i, _i, _i]),
     "clove_cuda_paged_prefill": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _f, _f, _i, _vp, _vp, _sz,
                                       _vp]),
+    "clove_cuda_qkv_packed_bytes": (_sz, [_i, _i]),
+    "clove_cuda_qkv_pack_weights": (_i, [_i, _vp, _i, _i, _vp, _vp]),
+    "clove_cuda_qkv_workspace_size": (_sz, [_vp, _i, _i, _i]),
+    "clove_cuda_qkv_append": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i, _vp, _f, _vp, _vp, _vp, _sz, _vp]),
     "clove_cuda_decode_status": (_i, [_vp, _vp, _ip]),
     "clove_cuda_set_decode_variant": (_i, [_i]),
     "clove_cuda_launch_count": (C.c_uint64, []),

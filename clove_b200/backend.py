@@ -83,6 +83,7 @@ class PagedAttention:
         self.w_k = Linear(dim, kv_dim, device, dtype, g)
         self.w_v = Linear(dim, kv_dim, device, dtype, g)
         self.w_o = Linear(dim, dim, device, torch.float32, g)
+        self._fused: tuple[torch.Tensor, torch.Tensor] | None = None
 
     def forward(self, x: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
                 context_lens: torch.Tensor, max_ctx: int | None = None) -> torch.Tensor:
@@ -91,6 +92,29 @@ class PagedAttention:
         v = self.w_v.forward(x)
         attn = CudaBackend.paged_attention(q, k, v, kv_cache, block_tables, context_lens, max_ctx=max_ctx)
         return self.w_o.forward(attn)
+
+    def fused_qkv(self, pool: KVPool) -> tuple[torch.Tensor, torch.Tensor]:
+        """The projection weights in clove_cuda_qkv_append's streaming layout
+        (W_q|W_k|W_v transposed, stacked and packed by the pool) and the f32
+        bias b_q|b_k|b_v.  Built once per weight update."""
+        if self._fused is None:
+            w = torch.cat([self.w_q.weight, self.w_k.weight, self.w_v.weight], dim=1).t().contiguous()
+            b = torch.cat([self.w_q.bias, self.w_k.bias, self.w_v.bias]).float().contiguous()
+            self._fused = (pool.pack_qkv_weights(w.to(pool.dtype)), b)
+        return self._fused
+
+    def forward_fused(self, x: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
+                      context_lens: torch.Tensor, max_ctx: int, rope_theta: float = 0.0) -> torch.Tensor:
+        """forward() with the three projections and the append in one
+        tensor-core kernel (16-bit caches): x [B, dim] in the cache dtype;
+        max_ctx bounds context_lens + 1.  Same result as forward() up to the
+        projections' rounding to the cache dtype."""
+        pool = CudaBackend._pool(kv_cache)
+        w, b = self.fused_qkv(pool)
+        q, lens = pool.qkv_append(x.to(pool.dtype).contiguous(), w, b, self.num_heads, block_tables, context_lens,
+                                  rope_theta=rope_theta)
+        attn = pool.decode(q, block_tables, lens, max_ctx=max_ctx)
+        return self.w_o.forward(attn.reshape(x.shape[0], -1))
 
     def prefill(self, x: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
                 context_lens: torch.Tensor, cu_seqlens: torch.Tensor, max_ctx: int,

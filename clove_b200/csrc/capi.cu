@@ -38,7 +38,7 @@ static int cuda_fail(const char* what, cudaError_t e) {
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point, so the
 // library does not link libcuda directly.
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -52,7 +52,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 static int encode_plane_map(CUtensorMap* map, void* base, const clove_pool& p, bool swizzled) {
-  auto fn = encode_fn();
+  auto fn = tensor_map_encoder();
   if (!fn) {
     set_last_error("cuTensorMapEncodeTiled unavailable from the driver");
     return CLOVE_ERR_CUDA;

@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -94,6 +95,9 @@ cudaError_t launch_dependent(Kern kern, unsigned grid, unsigned threads, size_t 
 int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                        const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
                        int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);
+
+// cuTensorMapEncodeTiled from the driver (null if unavailable)
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // error text / launch accounting (capi.cu)
 void set_last_error(const char* fmt, ...);

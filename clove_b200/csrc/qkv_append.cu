@@ -1,0 +1,608 @@
+// Fused Q/K/V projection + KV append for one decode step, on the 5th-generation
+// tensor cores (tcgen05, accumulator in tensor memory).
+//
+// The reference computes q = x Wq + bq, k = x Wk + bk, v = x Wv + bv with its
+// Linear layer (src/nn.rs:102-123, called from PagedAttention::forward at
+// src/nn.rs:538-540) and then hands k, v to the paged-attention op, which
+// must write them into the cache slot of each sequence's new token.  Here one
+// kernel does both: the GEMM epilogue adds the bias, optionally rotates q and
+// k (RoPE, the pairing of src/lazy.rs:4834-4842), writes q for the decode
+// and stores k, v straight into their cache slots, so K/V never make a round
+// trip through global memory.
+//
+// Shape of the work.  At decode the batch (M = 1..256 tokens per batch tile)
+// is small and the weights W [hidden, (Hq + 2 Hkv) D] are large: the kernel
+// streams the weights once, so HBM bandwidth bounds it.  The product is
+// computed transposed, D^T = W^T x^T: the 128-row tensor-core tile runs over
+// output features and the batch is the MMA's N dimension (16..256).  Both
+// operands are K-major in shared memory with the 128-byte swizzle: W^T is
+// stored [N_out, hidden] (rows of the reference's W laid out contiguously
+// along hidden), x is [M, hidden].
+//
+// Schedule (stream-K).  The work is (feature tile of 128) x (batch tile) x
+// (64-wide K block) units, split evenly and contiguously over one CTA per SM,
+// so every SM streams weights for the whole kernel whatever the tile count.
+// A CTA's range covers pieces ("segments") of one or more tiles.  A segment
+// that is a whole tile goes straight to the epilogue; otherwise its f32
+// partial goes to a workspace slot, and the CTA that completes the tile's
+// last piece (a per-tile arrival counter, reset by that CTA) sums the
+// partials in slot order and runs the epilogue.
+//
+// Roles in a CTA (192 threads): warp 0 lane 0 issues the bulk-tensor copies
+// (TMA) into a ring of stages; warp 1 lane 0 issues tcgen05.mma into one of
+// two tensor-memory accumulators (so one segment drains while the next
+// accumulates) and commits stages back to the producer; warps 2-5 (tensor-
+// memory lane groups 2, 3, 0, 1: one output feature per thread) drain
+// accumulators, add the bias, rotate, round, stage a tile's columns in shared
+// memory and write each column's 128 features — contiguous in q's row or in
+// the cache slot row — as 16-byte stores.  Every wait is bounded; a wait that
+// runs out sets CLOVE_FLAG_TIMEOUT in the pool's flag word and the CTA
+// finishes without hanging.
+#include <algorithm>
+#include <cmath>
+#include <type_traits>
+
+#include "../../include/clove_cuda.h"
+#include "common.cuh"
+#include "host.h"
+
+namespace clove {
+
+namespace {
+
+constexpr int kQkvThreads = 192;  // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
+constexpr int kEpiThreads = 128;
+constexpr int kTileN = 128;       // output features per tile (tensor-core M)
+constexpr int kTileK = 64;        // hidden elements per stage (one 128-byte swizzle row)
+constexpr int kMaxBatchTile = 256;
+constexpr size_t kSmemBudget = 224 * 1024;  // ring + output staging
+
+struct QkvArgs {
+  const void* w_packed;         // [ntiles_n][kb_total][128][64] pre-swizzled
+  const float* bias;            // [N] or null
+  const int32_t* block_tables;  // [M, bt_stride]
+  const int32_t* context_lens;  // [M] tokens cached before this one
+  int32_t* lens_out;            // [M] context_lens + 1, or null
+  void* q_out;                  // [M, Hq, D]
+  void* k_cache;
+  void* v_cache;
+  int32_t* flags;
+  float* partials;              // [tiles][max_contrib][batch_tile][128] f32
+  int32_t* counters;            // [tiles], zero between calls
+  int M, hidden, hq, hkv, D, bs, bt_stride, num_blocks;
+  int n_out;        // (hq + 2 hkv) * D
+  int kb_total;     // K blocks per tile
+  int ntiles_n;     // feature tiles
+  int batch_tile;   // MMA N (multiple of 16)
+  int nstage;
+  int max_contrib;  // partial slots per tile
+  int acc_cols;     // tensor-memory columns per accumulator (power of two >= 32)
+  long long units;  // tiles * kb_total
+  float rope_theta;
+  uint32_t wait_limit;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major tile with the 128-byte
+// swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte
+// offset), leading byte offset unused by this layout (encoded 1), descriptor
+// version 1 (bits 46-47), layout type 2 = 128-byte swizzle (bits 61-63).
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
+  return (uint64_t)((smem_addr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: f32 accumulate (bits 4-5 = 1), A and B
+// both bf16 (1) or both f16 (0) at bits 7-9 / 10-12, both K-major, N >> 3 at
+// bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ inline uint32_t qkv_idesc(bool bf16, int n) {
+  const uint32_t f = bf16 ? 1u : 0u;
+  return (1u << 4) | (f << 7) | (f << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTileN >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread completes.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive accumulator columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ T to_elem(float x);
+template <> __device__ __forceinline__ __nv_bfloat16 to_elem<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half to_elem<__half>(float x) { return __float2half_rn(x); }
+
+// First CTA whose unit range [g*U/G, (g+1)*U/G) contains unit x.
+__device__ __forceinline__ int first_cta(long long x, long long units, int grid) {
+  return (int)(((x + 1) * grid - 1) / units);
+}
+
+// Piece of a tile inside one CTA's unit range.
+struct Segment {
+  int tile, kb0, kb1;
+};
+
+__device__ __forceinline__ Segment segment_at(long long u, long long u_end, int kb_total) {
+  Segment s;
+  s.tile = (int)(u / kb_total);
+  s.kb0 = (int)(u - (long long)s.tile * kb_total);
+  s.kb1 = (int)min((long long)kb_total, (long long)s.kb0 + (u_end - u));
+  return s;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kQkvThreads, 1)
+    qkv_append_kernel(const __grid_constant__ CUtensorMap tm_x, const QkvArgs a) {
+  __shared__ __align__(8) uint64_t full_bar[16];
+  __shared__ __align__(8) uint64_t empty_bar[16];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ int last_flag;
+  extern __shared__ unsigned char smem_raw[];
+  // 1024-byte aligned (the swizzle atom), by offsetting the shared array
+  // itself so the compiler keeps the shared address space
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BT = a.batch_tile;
+  const uint32_t a_bytes = kTileN * 128, b_bytes = (uint32_t)BT * 128;
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+  T* stage_out = reinterpret_cast<T*>(smem + (size_t)a.nstage * stage_bytes);  // [BT][128] epilogue staging
+  const int G = gridDim.x;
+  const long long u_begin = (long long)blockIdx.x * a.units / G;
+  const long long u_end = (long long)(blockIdx.x + 1) * a.units / G;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.nstage; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiThreads);
+    }
+    fence_barrier_init();
+  }
+  __syncwarp();
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_slot)),
+                 "r"(2 * a.acc_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_slot;
+
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer: W^T tile [128 features, 64] and x tile [BT, 64] per stage
+      int i = 0;
+      bool ok = true;
+      for (long long u = u_begin; u < u_end && ok;) {
+        const Segment sg = segment_at(u, u_end, a.kb_total);
+        u += sg.kb1 - sg.kb0;
+        const int m0 = (sg.tile / a.ntiles_n) * kMaxBatchTile;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++i) {
+          const int s = i % a.nstage;
+          const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
+          if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1u, a.flags, a.wait_limit)) {
+            ok = false;
+            break;
+          }
+          unsigned char* st = smem + (size_t)s * stage_bytes;
+          mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
+          const int k0 = kb * kTileK;  // 64 elements = 128 bytes: meets the 16-byte rule
+          // the weight chunk of (feature tile, K block): 16 KB, contiguous and
+          // already in the swizzled order (clove_cuda_qkv_pack_weights)
+          bulk_load(st, static_cast<const unsigned char*>(a.w_packed) +
+                            ((size_t)(sg.tile % a.ntiles_n) * a.kb_total + kb) * a_bytes,
+                    a_bytes, &full_bar[s]);
+          tma_load_2d(st + a_bytes, &tm_x, &full_bar[s], k0, m0);
+        }
+      }
+      // drain: the last copies must land before the CTA exits
+      for (int t = max(0, i - a.nstage); t < i; ++t)
+        mbar_wait_bounded(&full_bar[t % a.nstage], (uint32_t)(t / a.nstage) & 1u, a.flags, a.wait_limit);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer: segment j accumulates in tensor-memory buffer j % 2
+      const uint32_t idesc = qkv_idesc(bf16, BT);
+      int i = 0, j = 0;
+      bool ok = true;
+      for (long long u = u_begin; u < u_end && ok; ++j) {
+        const Segment sg = segment_at(u, u_end, a.kb_total);
+        u += sg.kb1 - sg.kb0;
+        const int buf = j & 1;
+        const uint32_t use = (uint32_t)(j >> 1);
+        // the epilogue has drained this buffer's previous segment
+        ok = mbar_wait_bounded(&acc_empty[buf], (use & 1u) ^ 1u, a.flags, a.wait_limit);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(buf * a.acc_cols);
+        for (int kb = sg.kb0; kb < sg.kb1 && ok; ++kb, ++i) {
+          const int s = i % a.nstage;
+          const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
+          if (!mbar_wait_bounded(&full_bar[s], ph, a.flags, a.wait_limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + (size_t)s * stage_bytes);
+          const uint64_t da = sw128_kmajor_desc(sa), db = sw128_kmajor_desc(sa + a_bytes);
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k)  // 16 elements = 32 bytes = 2 descriptor units
+            umma_f16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb > sg.kb0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty_bar[s]);
+        }
+        umma_commit(&acc_full[buf]);  // arrives once the segment's MMAs complete
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue warps 2-5.  Thread e owns output feature r of the tile
+    // (its tensor-memory lane: warp w reads lanes 32 (w % 4) ..).
+    const int e = threadIdx.x - 64;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int qd = a.hq * a.D, kd = a.hkv * a.D;
+    int j = 0;
+    for (long long u = u_begin; u < u_end; ++j) {
+      const Segment sg = segment_at(u, u_end, a.kb_total);
+      u += sg.kb1 - sg.kb0;
+      const int tile_n = sg.tile % a.ntiles_n, m0 = (sg.tile / a.ntiles_n) * kMaxBatchTile;
+      const int n0 = tile_n * kTileN;
+      const int f = n0 + r;
+      const float bias = (a.bias && f < a.n_out) ? __ldg(a.bias + f) : 0.f;
+      const int d = f % a.D;
+      // RoPE angle factor for this feature's pair (2i, 2i+1): theta^(-2i/D)
+      // (warp-uniform: a warp's 32 features never straddle a head boundary)
+      const bool rot = a.rope_theta > 0.f && f < qd + kd;
+      const float inv_freq = rot ? powf(a.rope_theta, -2.f * (float)(d >> 1) / (float)a.D) : 0.f;
+      auto finish = [&](int c, float val) -> T {  // c: column within the batch tile
+        val += bias;
+        if (rot) {
+          // partner element of the pair lives in the neighbouring lane
+          const float other = __shfl_xor_sync(0xffffffffu, val, 1);
+          const int b = m0 + c;
+          const int pos = b < a.M ? __ldg(a.context_lens + b) : 0;
+          float sn, cs;
+          sincosf((float)pos * inv_freq, &sn, &cs);
+          val = (d & 1) ? other * sn + val * cs : val * cs - other * sn;
+        }
+        return to_elem<T>(val);
+      };
+
+      const int buf = j & 1;
+      const uint32_t use = (uint32_t)(j >> 1);
+      const bool ok = mbar_wait_bounded(&acc_full[buf], use & 1u, a.flags, a.wait_limit);
+      if (named_bar_or(1, kEpiThreads, !ok)) break;  // every epilogue warp leaves together
+      tc_fence_after();
+      const uint32_t acc = tmem + lane_off + (uint32_t)(buf * a.acc_cols);
+      if (sg.kb0 == 0 && sg.kb1 == a.kb_total) {
+        // the whole tile in this CTA
+        for (int c0 = 0; c0 < BT; c0 += 16) {
+          float v[16];
+          tmem_ld16(acc + (uint32_t)c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) stage_out[(c0 + i) * kTileN + r] = finish(c0 + i, v[i]);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+      } else {
+        // a piece: publish the partial in this CTA's slot of the tile
+        const long long t0 = (long long)sg.tile * a.kb_total;
+        const int g_first = first_cta(t0, a.units, G);
+        const int n_contrib = first_cta(t0 + a.kb_total - 1, a.units, G) - g_first + 1;
+        float* part = a.partials + (size_t)sg.tile * a.max_contrib * BT * kTileN;
+        float* mine = part + (size_t)(blockIdx.x - g_first) * BT * kTileN;
+        for (int c0 = 0; c0 < BT; c0 += 16) {
+          float v[16];
+          tmem_ld16(acc + (uint32_t)c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) __stcg(mine + (size_t)(c0 + i) * kTileN + r, v[i]);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        __threadfence();  // the partial is visible before this CTA's arrival is counted
+        named_bar_sync(1, kEpiThreads);
+        if (e == 0) last_flag = atomicAdd(a.counters + sg.tile, 1) == n_contrib - 1;
+        named_bar_sync(1, kEpiThreads);
+        if (!last_flag) continue;
+        // last piece of the tile: sum the partials in slot order
+        __threadfence();
+        if (e == 0) a.counters[sg.tile] = 0;  // zero again for the next call
+        for (int c0 = 0; c0 < BT; c0 += 8) {
+          float sum[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sum[i] = 0.f;
+          for (int p = 0; p < n_contrib; ++p) {
+            float t[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) t[i] = __ldcg(part + ((size_t)p * BT + c0 + i) * kTileN + r);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sum[i] += t[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) stage_out[(c0 + i) * kTileN + r] = finish(c0 + i, sum[i]);
+        }
+      }
+      named_bar_sync(1, kEpiThreads);  // staging complete
+      // 16-byte stores: 16 chunks of 8 features per column.  Section
+      // boundaries (q | k | v) are multiples of 64 features, so a chunk never
+      // straddles one.
+      for (int q = e; q < BT * 16; q += kEpiThreads) {
+        const int c = q >> 4, f0 = n0 + (q & 15) * 8;
+        const int b = m0 + c;
+        if (b >= a.M || f0 >= a.n_out) continue;
+        const uint4 val = *reinterpret_cast<const uint4*>(stage_out + (size_t)c * kTileN + (q & 15) * 8);
+        T* dst;
+        if (f0 < qd) {
+          if (tile_n == 0 && (q & 15) == 0 && a.lens_out) a.lens_out[b] = __ldg(a.context_lens + b) + 1;
+          dst = static_cast<T*>(a.q_out) + (size_t)b * qd + f0;
+        } else {
+          const int pos = __ldg(a.context_lens + b);
+          if (pos < 0 || pos / a.bs >= a.bt_stride) {
+            atomicOr(a.flags, CLOVE_FLAG_CTX_RANGE);
+            continue;
+          }
+          const int phys = __ldg(a.block_tables + (size_t)b * a.bt_stride + pos / a.bs);
+          if (phys < 0 || phys >= a.num_blocks) {
+            atomicOr(a.flags, CLOVE_FLAG_BLOCK_OOB);
+            continue;
+          }
+          const bool is_k = f0 < qd + kd;
+          dst = static_cast<T*>(is_k ? a.k_cache : a.v_cache) + ((size_t)phys * a.bs + pos % a.bs) * kd +
+                (f0 - (is_k ? qd : qd + kd));
+        }
+        __stcs(reinterpret_cast<uint4*>(dst), val);
+      }
+      named_bar_sync(1, kEpiThreads);  // staging free for the next tile
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * a.acc_cols)
+                 : "memory");
+  }
+}
+
+}  // namespace
+
+}  // namespace clove
+
+using namespace clove;
+
+// Encode a 2-D K-major operand map {hidden, rows} with a 64 x box_rows box and
+// the 128-byte swizzle.
+static int encode_operand_map(CUtensorMap* map, const void* base, int dtype, int hidden, int rows, int box_rows) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return CLOVE_ERR_CUDA;
+  const CUtensorMapDataType dt =
+      dtype == CLOVE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {(cuuint64_t)hidden, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)hidden * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kTileK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? CLOVE_OK : CLOVE_ERR_INVALID_ARG;
+}
+
+// One thread per 16-byte chunk of the packed layout: chunk (tile t, K block
+// kb, row r, position p) holds the 8 elements of W^T row t*128 + r, columns
+// kb*64 + 8 (p ^ (r % 8)) .. +7 — the 128-byte swizzle that the bulk-tensor
+// copies would apply — with zeros past n_out / hidden.
+template <typename T>
+__global__ void pack_weights_kernel(const T* __restrict__ w_t, T* __restrict__ out, int n_out, int hidden,
+                                    int kb_total, long long chunks) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < chunks;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int p = (int)(i & 7);
+    const int r = (int)((i >> 3) & 127);
+    const long long tk = i >> 10;  // t * kb_total + kb
+    const int kb = (int)(tk % kb_total), t = (int)(tk / kb_total);
+    const int row = t * kTileN + r, col0 = kb * kTileK + 8 * (p ^ (r & 7));
+    T v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int col = col0 + e;
+      v[e] = (row < n_out && col < hidden) ? w_t[(size_t)row * hidden + col] : T(0.f);
+    }
+    *reinterpret_cast<uint4*>(out + i * 8) = *reinterpret_cast<const uint4*>(v);
+  }
+}
+
+static size_t packed_bytes(int n_out, int hidden) {
+  return (size_t)((n_out + kTileN - 1) / kTileN) * ((hidden + kTileK - 1) / kTileK) * kTileN * kTileK * 2;
+}
+
+// Schedule and workspace of one call.
+struct QkvPlan {
+  int batch_tile, ntiles_n, n_btiles, kb_total, grid, max_contrib, nstage, acc_cols;
+  long long units;
+  size_t smem, off_partials, ws_bytes;
+};
+
+static QkvPlan plan_qkv(const clove_pool& pool, int batch, int hidden, int num_q_heads) {
+  QkvPlan P;
+  P.n_btiles = (batch + kMaxBatchTile - 1) / kMaxBatchTile;
+  P.batch_tile = P.n_btiles > 1 ? kMaxBatchTile : ((batch + 15) / 16) * 16;
+  const int n_out = (num_q_heads + 2 * pool.num_kv_heads) * pool.head_dim;
+  P.ntiles_n = (n_out + kTileN - 1) / kTileN;
+  P.kb_total = (hidden + kTileK - 1) / kTileK;
+  P.units = (long long)P.ntiles_n * P.n_btiles * P.kb_total;
+  // one CTA per SM, at least two K blocks each
+  P.grid = (int)std::max(1LL, std::min((long long)pool.num_sms, P.units / 2));
+  const long long per_cta = P.units / P.grid;  // shortest range
+  P.max_contrib = (int)std::min((long long)P.grid, (P.kb_total + per_cta - 1) / per_cta + 1);
+  P.acc_cols = P.batch_tile <= 32 ? 32 : P.batch_tile <= 64 ? 64 : P.batch_tile <= 128 ? 128 : 256;
+  const size_t stage = (size_t)kTileN * 128 + (size_t)P.batch_tile * 128;
+  const size_t staging = (size_t)P.batch_tile * kTileN * 2;
+  P.nstage = (int)std::min<size_t>(16, (kSmemBudget - staging) / stage);
+  P.smem = stage * P.nstage + staging + 1024;
+  const size_t tiles = (size_t)P.ntiles_n * P.n_btiles;
+  P.off_partials = (tiles * 4 + 255) & ~size_t(255);
+  P.ws_bytes = P.off_partials + tiles * P.max_contrib * P.batch_tile * kTileN * 4;
+  return P;
+}
+
+extern "C" {
+
+size_t clove_cuda_qkv_packed_bytes(int n_out, int hidden) {
+  if (n_out <= 0 || hidden <= 0) return 0;
+  return packed_bytes(n_out, hidden);
+}
+
+int clove_cuda_qkv_pack_weights(int dtype, const void* w_t, int n_out, int hidden, void* packed, void* stream) {
+  if ((dtype != CLOVE_DTYPE_BF16 && dtype != CLOVE_DTYPE_F16) || !w_t || !packed || n_out <= 0 || hidden <= 0 ||
+      (reinterpret_cast<uintptr_t>(packed) & 15u)) {
+    set_last_error("qkv_pack_weights: bf16/f16 weights, non-null pointers, packed 16-byte aligned");
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  const int kb_total = (hidden + kTileK - 1) / kTileK;
+  const long long chunks = (long long)packed_bytes(n_out, hidden) / 16;
+  const int blocks = (int)std::min<long long>((chunks + 255) / 256, 65535);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == CLOVE_DTYPE_BF16)
+    pack_weights_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(w_t),
+                                                              static_cast<__nv_bfloat16*>(packed), n_out, hidden,
+                                                              kb_total, chunks);
+  else
+    pack_weights_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(w_t), static_cast<__half*>(packed),
+                                                       n_out, hidden, kb_total, chunks);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error("qkv_pack_weights launch: %s", cudaGetErrorString(e));
+    return CLOVE_ERR_CUDA;
+  }
+  count_launches(1);
+  return CLOVE_OK;
+}
+
+size_t clove_cuda_qkv_workspace_size(clove_pool_t pool, int batch, int hidden, int num_q_heads) {
+  if (!pool || batch <= 0 || hidden <= 0 || num_q_heads <= 0) return 0;
+  return plan_qkv(*pool, batch, hidden, num_q_heads).ws_bytes;
+}
+
+int clove_cuda_qkv_append(clove_pool_t pool, const void* x, const void* w_packed, const float* bias, int batch,
+                          int hidden, int num_q_heads, const int32_t* block_tables, int bt_stride,
+                          const int32_t* context_lens, float rope_theta, void* q_out, int32_t* context_lens_out,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (!pool || batch < 0 || hidden <= 0 || num_q_heads <= 0 || bt_stride <= 0 || rope_theta < 0.f) {
+    set_last_error("qkv_append: bad arguments");
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  if (batch == 0) return CLOVE_OK;
+  if (!x || !w_packed || !block_tables || !context_lens || !q_out || !workspace ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u)) {
+    set_last_error("qkv_append: null pointer or workspace not 256-byte aligned");
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  if (pool->dtype == CLOVE_DTYPE_F32) {
+    set_last_error("qkv_append: the tensor-core projection takes bf16/f16 pools");
+    return CLOVE_ERR_UNSUPPORTED;
+  }
+  if (num_q_heads % pool->num_kv_heads || hidden % 8 ||
+      (reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(w_packed) & 15u) ||
+      (reinterpret_cast<uintptr_t>(q_out) & 15u)) {
+    set_last_error("qkv_append: num_q_heads must be a multiple of num_kv_heads, hidden of 8, x/w_packed/q_out 16-byte aligned");
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  const QkvPlan P = plan_qkv(*pool, batch, hidden, num_q_heads);
+  if (workspace_bytes < P.ws_bytes) {
+    set_last_error("qkv_append: workspace %zu bytes < required %zu", workspace_bytes, P.ws_bytes);
+    return CLOVE_ERR_WORKSPACE;
+  }
+  QkvArgs a = {};
+  a.w_packed = w_packed;
+  a.bias = bias;
+  a.block_tables = block_tables;
+  a.context_lens = context_lens;
+  a.lens_out = context_lens_out;
+  a.q_out = q_out;
+  a.k_cache = pool->k_cache;
+  a.v_cache = pool->v_cache;
+  a.flags = pool->flags;
+  a.counters = static_cast<int32_t*>(workspace);
+  a.partials = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + P.off_partials);
+  a.M = batch;
+  a.hidden = hidden;
+  a.hq = num_q_heads;
+  a.hkv = pool->num_kv_heads;
+  a.D = pool->head_dim;
+  a.bs = pool->block_size;
+  a.bt_stride = bt_stride;
+  a.num_blocks = pool->num_blocks;
+  a.n_out = (num_q_heads + 2 * pool->num_kv_heads) * pool->head_dim;
+  a.kb_total = P.kb_total;
+  a.ntiles_n = P.ntiles_n;
+  a.batch_tile = P.batch_tile;
+  a.nstage = P.nstage;
+  a.max_contrib = P.max_contrib;
+  a.acc_cols = P.acc_cols;
+  a.units = P.units;
+  a.rope_theta = rope_theta;
+  const uint32_t lim = debug_wait_limit();
+  a.wait_limit = lim ? lim : kWaitLimit;
+
+  CUtensorMap tm_x;
+  if (encode_operand_map(&tm_x, x, pool->dtype, hidden, batch, P.batch_tile) != CLOVE_OK) {
+    set_last_error("qkv_append: cuTensorMapEncodeTiled failed (hidden %d, batch %d)", hidden, batch);
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != pool->device) cudaSetDevice(pool->device);
+  auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_append_kernel<__nv_bfloat16> : qkv_append_kernel<__half>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem);
+  if (e == cudaSuccess)
+    kern<<<P.grid, kQkvThreads, P.smem, static_cast<cudaStream_t>(stream)>>>(tm_x, a);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (prev >= 0 && prev != pool->device) cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    set_last_error("qkv_append launch: %s", cudaGetErrorString(e));
+    return CLOVE_ERR_CUDA;
+  }
+  count_launches(1);
+  return CLOVE_OK;
+}
+
+}  // extern "C"

@@ -70,6 +70,7 @@ class KVPool:
             num_kv_heads, head_dim, _DTYPES[dtype], C.byref(h)))
         self.handle = h
         self._ws: torch.Tensor | None = None
+        self._qkv_ws: torch.Tensor | None = None  # fused projection scratch (kept zeroed by the kernel)
 
     @property
     def k_cache(self) -> torch.Tensor:
@@ -179,6 +180,53 @@ class KVPool:
 
     def append_decode(self, q, k_new, v_new, block_tables, context_lens, **kw) -> torch.Tensor:
         return self.decode(q, block_tables, context_lens, k_new=k_new, v_new=v_new, **kw)
+
+    def pack_qkv_weights(self, w_t: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """W^T [(Hq + 2 Hkv) D, hidden] (pool dtype; W_q|W_k|W_v transposed
+        and stacked) -> the fused projection's streaming layout (uint8)."""
+        if w_t.dim() != 2 or w_t.dtype != self.dtype or not w_t.is_contiguous() or w_t.device != self.device:
+            raise ValueError("w_t must be a contiguous [n_out, hidden] tensor of the pool's dtype and device")
+        n_out, hidden = w_t.shape
+        packed = torch.empty(int(self._lib.clove_cuda_qkv_packed_bytes(n_out, hidden)), dtype=torch.uint8,
+                             device=self.device)
+        _lib.check(self._lib.clove_cuda_qkv_pack_weights(_DTYPES[self.dtype], _ptr(w_t), n_out, hidden,
+                                                         _ptr(packed), _stream(stream)))
+        return packed
+
+    def qkv_append(self, x: torch.Tensor, w_packed: torch.Tensor, bias: torch.Tensor | None, num_q_heads: int,
+                   block_tables: torch.Tensor, context_lens: torch.Tensor, rope_theta: float = 0.0,
+                   q_out: torch.Tensor | None = None, lens_out: torch.Tensor | None = None,
+                   stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Fused Q/K/V projection + append: x [B, hidden] (pool dtype),
+        w_packed from pack_qkv_weights, bias f32 [(Hq + 2 Hkv) D] or None.
+        Stores k, v at slot context_lens[b] and returns (q [B, Hq, D] pool
+        dtype, context_lens + 1)."""
+        B = x.shape[0]
+        n_out = (num_q_heads + 2 * self.num_kv_heads) * self.head_dim
+        if x.dim() != 2 or x.dtype != self.dtype or not x.is_contiguous() or x.device != self.device:
+            raise ValueError("x must be a contiguous [batch, hidden] tensor of the pool's dtype and device")
+        hidden = x.shape[1]
+        if (w_packed.dtype != torch.uint8 or w_packed.device != self.device or not w_packed.is_contiguous()
+                or w_packed.numel() != int(self._lib.clove_cuda_qkv_packed_bytes(n_out, hidden))):
+            raise ValueError("w_packed must come from pack_qkv_weights for this shape")
+        if bias is not None and (bias.shape != (n_out,) or bias.dtype != torch.float32 or not bias.is_contiguous()):
+            raise ValueError(f"bias must be f32 [{n_out}]")
+        self._check_i32(block_tables, "block_tables")
+        self._check_i32(context_lens, "context_lens")
+        if q_out is None:
+            q_out = torch.empty((B, num_q_heads, self.head_dim), dtype=self.dtype, device=self.device)
+        if lens_out is None:
+            lens_out = torch.empty(B, dtype=torch.int32, device=self.device)
+        n = int(self._lib.clove_cuda_qkv_workspace_size(self.handle, B, hidden, num_q_heads))
+        if self._qkv_ws is None or self._qkv_ws.numel() < n:
+            if self._qkv_ws is not None:
+                torch.cuda.current_stream(self.device).synchronize()  # queued calls may still use the old one
+            self._qkv_ws = torch.zeros(max(n, 256), dtype=torch.uint8, device=self.device)  # zero-filled: counters
+        _lib.check(self._lib.clove_cuda_qkv_append(
+            self.handle, _ptr(x), _ptr(w_packed), _ptr(bias), B, hidden, num_q_heads, _ptr(block_tables),
+            block_tables.shape[1], _ptr(context_lens), float(rope_theta), _ptr(q_out), _ptr(lens_out),
+            _ptr(self._qkv_ws), self._qkv_ws.numel(), _stream(stream)))
+        return q_out, lens_out
 
     def prefill(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
                 block_tables: torch.Tensor, context_lens: torch.Tensor, max_ctx: int, scale: float | None = None,

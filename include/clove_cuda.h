@@ -189,6 +189,49 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k,
                              void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* Fused Q/K/V projection + KV append (one decode step) on the tensor cores.
+ * Replaces the three Linear calls of PagedAttention::forward
+ * (src/nn.rs:538-540; Linear y = x W + b, src/nn.rs:102-123) and the append
+ * that the paged-attention op must do with their k, v.
+ *
+ * Weights are packed once (per weight update) into the kernel's streaming
+ * layout: clove_cuda_qkv_pack_weights takes W^T [n_out, hidden] (pool dtype,
+ * row-major: the reference's W_q | W_k | W_v, each [hidden, out],
+ * transposed and stacked; n_out = (num_q_heads + 2 num_kv_heads) * head_dim)
+ * and writes clove_cuda_qkv_packed_bytes(n_out, hidden) bytes: 128-feature x
+ * 64-element tiles, each 16 KB contiguous in the 128-byte-swizzled order the
+ * tensor cores read, zero-padded at the edges.
+ *
+ * clove_cuda_qkv_append:
+ *   x         [batch, hidden], pool dtype (bf16/f16), 16-byte aligned
+ *   w_packed  the packed weights above, 16-byte aligned
+ *   bias      f32 [n_out] (b_q | b_k | b_v), or null
+ * Writes q_out [batch, num_q_heads, head_dim] (pool dtype, 16-byte aligned)
+ * and stores k, v at slot context_lens[b] of sequence b through
+ * block_tables.  With rope_theta > 0, q and k are rotated by position
+ * context_lens[b] (the pairing of clove_cuda_paged_prefill).
+ * context_lens_out (optional, int32 [batch]) receives context_lens + 1: the
+ * lengths to decode over with clove_cuda_paged_decode.  Bad slots are
+ * skipped and flagged in the pool's status word, like
+ * clove_cuda_reshape_and_cache.  Scratch: clove_cuda_qkv_workspace_size
+ * bytes, 256-byte aligned, ZERO-FILLED before its first use; every call
+ * that completes leaves it zeroed again (its per-tile counters), so one
+ * buffer serves all later calls on a stream.  f32 pools return
+ * CLOVE_ERR_UNSUPPORTED. */
+size_t clove_cuda_qkv_packed_bytes(int n_out, int hidden);
+int clove_cuda_qkv_pack_weights(int dtype, const void* w_t, int n_out,
+                                int hidden, void* packed, void* stream);
+size_t clove_cuda_qkv_workspace_size(clove_pool_t pool, int batch, int hidden,
+                                     int num_q_heads);
+int clove_cuda_qkv_append(clove_pool_t pool, const void* x,
+                          const void* w_packed, const float* bias, int batch,
+                          int hidden, int num_q_heads,
+                          const int32_t* block_tables, int bt_stride,
+                          const int32_t* context_lens, float rope_theta,
+                          void* q_out, int32_t* context_lens_out,
+                          void* workspace, size_t workspace_bytes,
+                          void* stream);
+
 /* Append + decode for callers that cannot allocate device memory when they
  * decode (an engine that hands all of HBM to its KV pool at start-up, a host
  * whose device memory comes only from an allocator it may not call on the

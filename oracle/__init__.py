@@ -165,3 +165,27 @@ def rope(x: np.ndarray, positions, theta: float) -> np.ndarray:
     out[..., 0::2] = x0 * c - x1 * s
     out[..., 1::2] = x0 * s + x1 * c
     return out
+
+
+def linear(x: np.ndarray, w: np.ndarray, b: np.ndarray | None) -> np.ndarray:
+    """float64 y = x W + b, the reference Linear (src/nn.rs:102-123:
+    matmul(x, weights) then add(bias)); W is [in, out] as the reference
+    stores it."""
+    y = np.asarray(x, np.float64) @ np.asarray(w, np.float64)
+    return y if b is None else y + np.asarray(b, np.float64)
+
+
+def qkv_append(x, w_q, w_k, w_v, b_q, b_k, b_v, num_q_heads: int, num_kv_heads: int, positions,
+               rope_theta: float = 0.0):
+    """The projections of PagedAttention::forward (src/nn.rs:538-540) in
+    float64, optionally rotated (RoPE) at each row's position: returns
+    q [B, Hq, D], k [B, Hkv, D], v [B, Hkv, D] before rounding to the pool's
+    element type.  The fused kernel writes k, v at slot positions[b]."""
+    B = np.asarray(x).shape[0]
+    q = linear(x, w_q, b_q).reshape(B, num_q_heads, -1)
+    k = linear(x, w_k, b_k).reshape(B, num_kv_heads, -1)
+    v = linear(x, w_v, b_v).reshape(B, num_kv_heads, -1)
+    if rope_theta > 0:
+        q = rope(q, positions, rope_theta)
+        k = rope(k, positions, rope_theta)
+    return q, k, v
