@@ -364,6 +364,121 @@ def run_ours(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_qkv(args) -> None:
+    """`--op qkv_append`: the fused Q/K/V projection + KV append
+    (clove_cuda_qkv_append) on one GPU, shaped like config C3's decode step
+    (hidden 4096 = 32 x 128, 32 q / 8 kv heads, bf16, batch 128 unless
+    --batch).  Four packed weight copies rotate (201 MB > L2), so each step
+    streams its weights from HBM.  Reports the kernel's weight-streaming
+    bandwidth against the measured HBM peak, and the same step done as a
+    cuBLAS GEMM + the append kernel for comparison."""
+    import torch
+
+    from clove_b200 import KVPool, launch_count
+    ws, rank, local = _dist()
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    hidden, hq, hkv, D, bs = 4096, 32, 8, 128, 16
+    B = args.batch or 128
+    n_out = (hq + 2 * hkv) * D
+    g = torch.Generator(device=dev)
+    g.manual_seed(303)
+    pool = KVPool(B * 4 + 8, bs, hkv, D, torch.bfloat16, dev)
+    x = torch.randn((B, hidden), device=dev, generator=g).bfloat16()
+    raw = [(torch.randn((n_out, hidden), device=dev, generator=g) / 64).bfloat16() for _ in range(4)]
+    packed = [pool.pack_qkv_weights(w) for w in raw]
+    bias = torch.randn(n_out, device=dev, generator=g) * 0.1
+    bt = torch.arange(B * 4, device=dev, dtype=torch.int32).reshape(B, 4)
+    ctx = torch.randint(0, 4 * bs, (B,), device=dev, dtype=torch.int32, generator=g)
+    q = torch.empty((B, hq, D), dtype=torch.bfloat16, device=dev)
+    lens = torch.empty(B, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+
+    def graph_of(fns, reps):
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for f in fns:
+                f()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for i in range(reps):
+                fns[i % len(fns)]()
+        return gr
+
+    def timed(gr, reps):
+        for _ in range(max(args.warmup, 3)):
+            gr.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record()
+        for _ in range(args.steps):
+            gr.replay()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / (args.steps * reps)  # ms per step
+
+    REPS = 20
+    fused = [lambda w=w: pool.qkv_append(x, w, bias, hq, bt, ctx, q_out=q, lens_out=lens) for w in packed]
+    gr = graph_of(fused, REPS)
+    n0 = launch_count()
+    fused[0]()  # launches per step, counted on one eager call (graph replays bypass the host)
+    per_step = launch_count() - n0
+    with ClockSampler(local) as clk:
+        ms = timed(gr, REPS)
+    launches = per_step * args.steps * REPS
+    assert pool.pool_status() == 0
+    # library comparison: one cuBLAS GEMM (bias folded in) + the append kernel
+    y = torch.empty((B, n_out), dtype=torch.bfloat16, device=dev)
+    slots = (bt[torch.arange(B, device=dev), (ctx // bs).long()] * bs + ctx % bs).to(torch.int32)
+    bb = bias.bfloat16()
+
+    def lib_step(w):
+        torch.addmm(bb, x, w.t(), out=y)
+        pool.reshape_and_cache(y[:, hq * D:(hq + hkv) * D].contiguous(), y[:, (hq + hkv) * D:].contiguous(), slots)
+
+    ms_lib = timed(graph_of([lambda w=w: lib_step(w) for w in raw], REPS), REPS)
+    # end to end: x from pinned host memory, q back to the host, every step
+    xh = x.cpu().pin_memory()
+    qh = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    for _ in range(3):
+        x.copy_(xh, non_blocking=True)
+        pool.qkv_append(x, packed[0], bias, hq, bt, ctx, q_out=q, lens_out=lens)
+        qh.copy_(q, non_blocking=True)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+    steps_e2e = min(args.steps, 200)
+    a.record()
+    for i in range(steps_e2e):
+        x.copy_(xh, non_blocking=True)
+        pool.qkv_append(x, packed[i % 4], bias, hq, bt, ctx, q_out=q, lens_out=lens)
+        qh.copy_(q, non_blocking=True)
+    b.record()
+    b.synchronize()
+    ms_e2e = a.elapsed_time(b) / steps_e2e
+    w_bytes = packed[0].numel()
+    alg = w_bytes + x.numel() * 2 + n_out * 4 + B * n_out * 2 + B * 4 * 3  # weights, x, bias, q/k/v out, tables
+    peak, kind = _peaks()
+    achieved = alg / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "fused_qkv_append_tokens_per_s", "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"C3-shaped decode projection: x [{B}, {hidden}] -> q/k/v {hq}q/{hkv}kv x {D}, "
+                               f"bf16, K/V into paged slots (bs {bs})",
+                   "l2": "4 weight copies rotated (201 MB > L2)", "graph": True},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_kind": kind},
+        "library_step_ms": ms_lib, "library_step": "torch.addmm (cuBLAS) + clove reshape_and_cache",
+        "e2e": {"value": B / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 2,
+                "d2h_bytes_per_step": q.numel() * 2},
+        "gpu_launches": launches, "clocks": clk.summary(),
+    }))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -371,6 +486,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2")
+    ap.add_argument("--op", default="decode", choices=["decode", "qkv_append"],
+                    help="decode (the headline path) or the fused Q/K/V projection + append")
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--batch", type=int, default=None, help="override the config batch (profiling only)")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a captured CUDA graph")
@@ -378,7 +495,9 @@ def main() -> None:
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per decode launch from an ncu capture (reported as roofline.traffic)")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.op == "qkv_append":
+        run_qkv(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

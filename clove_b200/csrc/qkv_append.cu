@@ -67,7 +67,7 @@ struct QkvArgs {
   void* k_cache;
   void* v_cache;
   int32_t* flags;
-  float* partials;              // [tiles][max_contrib][batch_tile][128] f32
+  float* partials;              // [tiles][max_contrib][128][batch_tile] f32
   int32_t* counters;            // [tiles], zero between calls
   int M, hidden, hq, hkv, D, bs, bt_stride, num_blocks;
   int n_out;        // (hq + 2 hkv) * D
@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int last_flag;
+  __shared__ int32_t slot_of[kMaxBatchTile];  // cache row of each batch column of the current tile (-1: skip)
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte aligned (the swizzle atom), by offsetting the shared array
   // itself so the compiler keeps the shared address space
@@ -313,6 +314,24 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       const bool ok = mbar_wait_bounded(&acc_full[buf], use & 1u, a.flags, a.wait_limit);
       if (named_bar_or(1, kEpiThreads, !ok)) break;  // every epilogue warp leaves together
       tc_fence_after();
+      // cache slot of each column, once per tile (read by the stores below,
+      // after the staging barrier)
+      for (int c = e; c < BT; c += kEpiThreads) {
+        const int b = m0 + c;
+        int slot = -1;
+        if (b < a.M) {
+          const int pos = __ldg(a.context_lens + b);
+          if (pos < 0 || pos / a.bs >= a.bt_stride) {
+            if (tile_n == 0) atomicOr(a.flags, CLOVE_FLAG_CTX_RANGE);
+          } else {
+            const int phys = __ldg(a.block_tables + (size_t)b * a.bt_stride + pos / a.bs);
+            if (phys >= 0 && phys < a.num_blocks) slot = phys * a.bs + pos % a.bs;
+            else if (tile_n == 0) atomicOr(a.flags, CLOVE_FLAG_BLOCK_OOB);
+          }
+          if (tile_n == 0 && a.lens_out) a.lens_out[b] = pos + 1;
+        }
+        slot_of[c] = slot;
+      }
       const uint32_t acc = tmem + lane_off + (uint32_t)(buf * a.acc_cols);
       if (sg.kb0 == 0 && sg.kb1 == a.kb_total) {
         // the whole tile in this CTA
@@ -331,11 +350,15 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         const int n_contrib = first_cta(t0 + a.kb_total - 1, a.units, G) - g_first + 1;
         float* part = a.partials + (size_t)sg.tile * a.max_contrib * BT * kTileN;
         float* mine = part + (size_t)(blockIdx.x - g_first) * BT * kTileN;
+        // feature-major [slot][feature][column]: each thread moves its own
+        // columns with 16-byte accesses
+        float* my_row = mine + (size_t)r * BT;
         for (int c0 = 0; c0 < BT; c0 += 16) {
           float v[16];
           tmem_ld16(acc + (uint32_t)c0, v);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) __stcg(mine + (size_t)(c0 + i) * kTileN + r, v[i]);
+          for (int i = 0; i < 16; i += 4)
+            __stcg(reinterpret_cast<float4*>(my_row + c0 + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[buf]);
@@ -347,19 +370,26 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         // last piece of the tile: sum the partials in slot order
         __threadfence();
         if (e == 0) a.counters[sg.tile] = 0;  // zero again for the next call
-        for (int c0 = 0; c0 < BT; c0 += 8) {
-          float sum[8];
+        for (int c0 = 0; c0 < BT; c0 += 16) {
+          float sum[16];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) sum[i] = 0.f;
+          for (int i = 0; i < 16; ++i) sum[i] = 0.f;
+#pragma unroll 2
           for (int p = 0; p < n_contrib; ++p) {
-            float t[8];
+            const float4* src = reinterpret_cast<const float4*>(part + ((size_t)p * kTileN + r) * BT + c0);
+            float4 t[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) t[i] = __ldcg(part + ((size_t)p * BT + c0 + i) * kTileN + r);
+            for (int i = 0; i < 4; ++i) t[i] = __ldcg(src + i);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) sum[i] += t[i];
+            for (int i = 0; i < 4; ++i) {
+              sum[4 * i] += t[i].x;
+              sum[4 * i + 1] += t[i].y;
+              sum[4 * i + 2] += t[i].z;
+              sum[4 * i + 3] += t[i].w;
+            }
           }
 #pragma unroll
-          for (int i = 0; i < 8; ++i) stage_out[(c0 + i) * kTileN + r] = finish(c0 + i, sum[i]);
+          for (int i = 0; i < 16; ++i) stage_out[(c0 + i) * kTileN + r] = finish(c0 + i, sum[i]);
         }
       }
       named_bar_sync(1, kEpiThreads);  // staging complete
@@ -373,22 +403,12 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         const uint4 val = *reinterpret_cast<const uint4*>(stage_out + (size_t)c * kTileN + (q & 15) * 8);
         T* dst;
         if (f0 < qd) {
-          if (tile_n == 0 && (q & 15) == 0 && a.lens_out) a.lens_out[b] = __ldg(a.context_lens + b) + 1;
           dst = static_cast<T*>(a.q_out) + (size_t)b * qd + f0;
         } else {
-          const int pos = __ldg(a.context_lens + b);
-          if (pos < 0 || pos / a.bs >= a.bt_stride) {
-            atomicOr(a.flags, CLOVE_FLAG_CTX_RANGE);
-            continue;
-          }
-          const int phys = __ldg(a.block_tables + (size_t)b * a.bt_stride + pos / a.bs);
-          if (phys < 0 || phys >= a.num_blocks) {
-            atomicOr(a.flags, CLOVE_FLAG_BLOCK_OOB);
-            continue;
-          }
+          const int slot = slot_of[c];
+          if (slot < 0) continue;
           const bool is_k = f0 < qd + kd;
-          dst = static_cast<T*>(is_k ? a.k_cache : a.v_cache) + ((size_t)phys * a.bs + pos % a.bs) * kd +
-                (f0 - (is_k ? qd : qd + kd));
+          dst = static_cast<T*>(is_k ? a.k_cache : a.v_cache) + (size_t)slot * kd + (f0 - (is_k ? qd : qd + kd));
         }
         __stcs(reinterpret_cast<uint4*>(dst), val);
       }
