@@ -1,0 +1,61 @@
+"""CPU: the lazy planner turns a traced PagedAttention node into a step sized
+from the kv_cache shape (head_dim, block_size, KV heads), where the
+reference's planner reads head_dim from q's last dimension and fixes the
+block size at 16 (src/lazy.rs:2369-2372, :2384)."""
+import pytest
+
+from clove_b200.lazy import LazyBackend, Opcode, PagedAttentionStep, compile
+
+
+def _trace(q_shape, kv_shape, with_projection=False):
+    lb = LazyBackend()
+    B = q_shape[0]
+    if with_projection:
+        x = lb.input("x", (B, 4096))
+        wq, bq = lb.input("wq", (4096, 4096)), lb.input("bq", (4096,))
+        q = lb.add(lb.matmul(x, wq), bq)
+    else:
+        q = lb.input("q", q_shape)
+    k = lb.input("k", (B, kv_shape[-2] * kv_shape[-1]))
+    v = lb.input("v", (B, kv_shape[-2] * kv_shape[-1]))
+    kv = lb.input("kv_cache", kv_shape)
+    bt = lb.input("block_tables", (B, 64))
+    cl = lb.input("context_lens", (B,))
+    out = lb.paged_attention(q, k, v, kv, bt, cl)
+    return lb, out
+
+
+def test_node_shape_is_q_shape_and_step_sizes_come_from_the_cache():
+    lb, out = _trace(("B", 64 * 128), (2, 40960, 32, 8, 128))
+    assert out.shape == ("B", 64 * 128)
+    (st,) = compile(lb.graph, [out])
+    assert isinstance(st, PagedAttentionStep)
+    # the reference's planner would say head_dim 8192 (q's last dim) and block 16
+    assert (st.head_dim, st.block_size, st.num_kv_heads, st.num_q_heads) == (128, 32, 8, 64)
+    assert st.deps == [n.id for n in lb.graph.nodes[:6]]
+
+
+def test_three_dim_q_and_projection_chain_order():
+    lb, out = _trace((16, 32, 128), (2, 1024, 16, 8, 128), with_projection=True)
+    steps = compile(lb.graph, [out])
+    # the projection's MatMul + bias Add plan as one Linear step
+    assert [s.op for s in steps] == [Opcode.LINEAR, Opcode.PAGED_ATTENTION]
+    assert steps[-1].num_q_heads == 32
+
+
+@pytest.mark.parametrize("q_shape,kv_shape,msg", [
+    ((4, 100), (2, 64, 16, 2, 64), "multiple of head_dim"),
+    ((4, 3 * 64), (2, 64, 16, 2, 64), "multiple of num_kv_heads"),
+    ((4, 128), (64, 16, 2, 64), "kv_cache must be"),
+    ((4, 128), (2, 64, "bs", 2, 64), "block_size must be a constant"),
+])
+def test_planner_rejects_inconsistent_shapes(q_shape, kv_shape, msg):
+    lb, out = _trace(q_shape, kv_shape)
+    with pytest.raises(ValueError, match=msg):
+        compile(lb.graph, [out])
+
+
+def test_unused_nodes_are_not_planned():
+    lb, out = _trace((4, 128), (2, 64, 16, 2, 64))
+    lb.matmul(lb.input("a", (4, 4)), lb.input("b", (4, 4)))  # dead branch
+    assert [s.op for s in compile(lb.graph, [out])] == [Opcode.PAGED_ATTENTION]
