@@ -40,6 +40,9 @@
 // finishes without hanging.
 #include <algorithm>
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <type_traits>
 
 #include "../../include/clove_cuda.h"
@@ -52,6 +55,9 @@ namespace {
 
 constexpr int kQkvThreads = 192;  // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
 constexpr int kEpiThreads = 128;
+constexpr int kClusterThreads = 256;  // cluster schedule: warp 0 copies, warp 1 MMAs, all 8 in the epilogue
+constexpr int kStreamKMaxTile = 32;   // batch tiles up to this use stream-K, larger ones the cluster schedule
+constexpr size_t kRingBudget = 200 * 1024;  // cluster schedule: ring bytes (its epilogue buffers overlay it)
 constexpr int kTileN = 128;       // output features per tile (tensor-core M)
 constexpr int kTileK = 64;        // hidden elements per stage (one 128-byte swizzle row)
 constexpr int kMaxBatchTile = 256;
@@ -76,6 +82,7 @@ struct QkvArgs {
   int batch_tile;   // MMA N (multiple of 16)
   int nstage;
   int max_contrib;  // partial slots per tile
+  int splits;       // cluster schedule: K splits (cluster size)
   int acc_cols;     // tensor-memory columns per accumulator (power of two >= 32)
   long long units;  // tiles * kb_total
   float rope_theta;
@@ -136,6 +143,28 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of `p` (this CTA's shared memory) in the shared window of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_peer(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float x, float y, float z, float w) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x), "f"(y), "f"(z), "f"(w)
+               : "memory");
 }
 
 template <typename T>
@@ -424,11 +453,262 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   }
 }
 
+// Cluster schedule for batch tiles above 32 columns: grid (feature tiles) x
+// (K splits) x (batch tiles), the K splits of a feature tile forming one
+// thread-block cluster.  Each CTA accumulates its K range in tensor memory;
+// the CTAs then push each other's columns through distributed shared memory
+// (CTA j owns a 1/splits slice of the batch columns) and each runs the
+// epilogue for its slice, so the reduction is spread over the cluster.
+// 256 threads: warp 0 copies, warp 1 MMAs, warps 2-7 look up the cache slots;
+// all 8 warps drain (warp w reads tensor-memory lanes 32 (w % 4) .., for
+// alternating 16-column chunks) and store.
+template <typename T>
+__global__ void __launch_bounds__(kClusterThreads, 1)
+    qkv_cluster_kernel(const __grid_constant__ CUtensorMap tm_x, const QkvArgs a) {
+  __shared__ __align__(8) uint64_t full_bar[16];
+  __shared__ __align__(8) uint64_t empty_bar[16];
+  __shared__ __align__(8) uint64_t done_bar;
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ int32_t slot_of[kMaxBatchTile];  // cache row of each batch column (-1: skip)
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_n = blockIdx.x, split = blockIdx.y, tile_m = blockIdx.z;
+  const int n0 = tile_n * kTileN, m0 = tile_m * kMaxBatchTile;
+  const int BT = a.batch_tile;
+  const uint32_t a_bytes = kTileN * 128, b_bytes = (uint32_t)BT * 128;
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+  // this split's range of 64-wide K blocks
+  const int kb_per = a.kb_total / a.splits, kb_rem = a.kb_total % a.splits;
+  const int kb0 = split * kb_per + min(split, kb_rem);
+  const int nkb = kb_per + (split < kb_rem ? 1 : 0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.nstage; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&done_bar, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  if (warp == 0) {
+    // tensor-memory columns: a power of two >= 32 covering the batch tile
+    const uint32_t ncols = BT <= 32 ? 32u : BT <= 64 ? 64u : BT <= 128 ? 128u : 256u;
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_slot;
+
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer: W^T tile [128 features, 64] and x tile [BT, 64] per stage
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % a.nstage;
+        const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
+        if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1u, a.flags, a.wait_limit)) break;
+        unsigned char* st = smem + (size_t)s * stage_bytes;
+        mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
+        const int k0 = (kb0 + i) * kTileK;  // 64 elements = 128 bytes: meets the 16-byte rule
+        // the weight chunk of (feature tile, K block): 16 KB, contiguous, pre-swizzled
+        bulk_load(st, static_cast<const unsigned char*>(a.w_packed) + ((size_t)tile_n * a.kb_total + kb0 + i) * a_bytes,
+                  a_bytes, &full_bar[s]);
+        tma_load_2d(st + a_bytes, &tm_x, &full_bar[s], k0, m0);
+        ++issued;
+      }
+      // drain: the copies issued last must have landed before shared memory is reused
+      for (int i = max(0, issued - a.nstage); i < issued; ++i)
+        mbar_wait_bounded(&full_bar[i % a.nstage], (uint32_t)(i / a.nstage) & 1u, a.flags, a.wait_limit);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer
+      const uint32_t idesc = qkv_idesc(bf16, BT);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % a.nstage;
+        const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
+        if (!mbar_wait_bounded(&full_bar[s], ph, a.flags, a.wait_limit)) break;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + (size_t)s * stage_bytes);
+        const uint64_t da = sw128_kmajor_desc(sa), db = sw128_kmajor_desc(sa + a_bytes);
+#pragma unroll
+        for (int k = 0; k < kTileK / 16; ++k)  // 16 elements = 32 bytes = 2 descriptor units
+          umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&empty_bar[s]);
+      }
+      umma_commit(&done_bar);
+    }
+    __syncwarp();
+  } else {
+    // warps 2-3, idle during the main loop: the cache slot of each batch
+    // column from its sequence's block table (read after the barrier below)
+    for (int c = threadIdx.x - 64; c < BT; c += kClusterThreads - 64) {  // warps 2-7
+      const int b = m0 + c;
+      int slot = -1;
+      if (b < a.M) {
+        const int pos = __ldg(a.context_lens + b);
+        if (pos < 0 || pos / a.bs >= a.bt_stride) {
+          atomicOr(a.flags, CLOVE_FLAG_CTX_RANGE);
+        } else {
+          const int phys = __ldg(a.block_tables + (size_t)b * a.bt_stride + pos / a.bs);
+          if (phys < 0 || phys >= a.num_blocks) atomicOr(a.flags, CLOVE_FLAG_BLOCK_OOB);
+          else slot = phys * a.bs + pos % a.bs;
+        }
+        if (a.lens_out && tile_n == 0 && split == 0) a.lens_out[b] = pos + 1;
+      }
+      slot_of[c] = slot;
+    }
+  }
+
+  // ---- epilogue.  Thread t computes feature r = t % 128 (its tensor-memory
+  // lane) for the columns of its half h = t / 128 (alternating 16-column
+  // chunks), rounds, and stages the result in shared memory as
+  // stage[c][128] (pool dtype); the CTA then writes each column's 128
+  // features — contiguous in q's row or in the cache slot row — as 16-byte
+  // vectors.
+  const int r = threadIdx.x & (kTileN - 1), half = threadIdx.x >> 7;
+  const int f = n0 + r;
+  const int qd = a.hq * a.D, kd = a.hkv * a.D;
+  const float bias = (a.bias && f < a.n_out) ? __ldg(a.bias + f) : 0.f;
+  const int d = f % a.D;
+  // RoPE angle factor for this feature's pair (2i, 2i+1): theta^(-2i/D)
+  // (warp-uniform: a warp's 32 features never straddle a head boundary)
+  const bool rot = a.rope_theta > 0.f && f < qd + kd;
+  const float inv_freq = rot ? powf(a.rope_theta, -2.f * (float)(d >> 1) / (float)a.D) : 0.f;
+  auto finish = [&](int c, float val) -> T {  // c: column within the batch tile
+    val += bias;
+    if (rot) {
+      // partner element of the pair lives in the neighbouring lane
+      const float other = __shfl_xor_sync(0xffffffffu, val, 1);
+      const int b = m0 + c;
+      const int pos = b < a.M ? __ldg(a.context_lens + b) : 0;
+      float sn, cs;
+      sincosf((float)pos * inv_freq, &sn, &cs);
+      val = (d & 1) ? other * sn + val * cs : val * cs - other * sn;
+    }
+    return to_elem<T>(val);
+  };
+
+  mbar_wait_bounded(&done_bar, 0, a.flags, a.wait_limit);
+  tc_fence_after();
+  const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+  const int S = a.splits;
+  int c_lo = 0, n_c = BT;  // this CTA's columns
+  T* stage_out;
+  if (S == 1) {
+    stage_out = reinterpret_cast<T*>(smem);
+    for (int c0 = 16 * half; c0 < BT; c0 += 32) {
+      float v[16];
+      tmem_ld16(t_lane + (uint32_t)c0, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) stage_out[(c0 + i) * kTileN + r] = finish(c0 + i, v[i]);
+    }
+    tc_fence_before();
+    __syncthreads();  // staging and slot_of complete
+  } else {
+    // ---- split-K reduction across the cluster.  CTA j owns the batch
+    // columns [j*cs, (j+1)*cs) (cs a multiple of 16); every CTA pushes its
+    // partial sums of those columns into CTA j's receive buffer
+    // recv[src][feature][cs + 4] (f32, overlaying the ring; the 4-float pad
+    // keeps 16-byte accesses of consecutive features on distinct banks), so
+    // each value crosses the cluster once, with 16-byte stores.
+    const uint32_t rank = cluster_rank();
+    const int cs = ((BT + S - 1) / S + 15) & ~15;
+    const int pitch = cs + 4;
+    float* recv = reinterpret_cast<float*>(smem);
+    stage_out = reinterpret_cast<T*>(smem + (size_t)S * kTileN * pitch * 4);
+    // every CTA of the cluster has finished its main loop before anyone
+    // writes into another's ring
+    cluster_sync();
+    for (int c0 = 16 * half; c0 < BT; c0 += 32) {
+      float v[16];
+      tmem_ld16(t_lane + (uint32_t)c0, v);
+      const int owner = c0 / cs;
+      float* dst = recv + ((size_t)rank * kTileN + r) * pitch + (c0 - owner * cs);
+      const uint32_t da = map_peer(dst, (uint32_t)owner);
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) st_cluster_v4(da + 4u * i, v[i], v[i + 1], v[i + 2], v[i + 3]);
+    }
+    tc_fence_before();
+    cluster_sync();  // pushes visible; no shared memory is touched remotely after this
+    c_lo = (int)rank * cs;
+    n_c = max(0, min(cs, BT - c_lo));
+    for (int j = 4 * half; j < n_c; j += 8) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < S; ++p) {
+        const float4 x4 = *reinterpret_cast<const float4*>(recv + ((size_t)p * kTileN + r) * pitch + j);
+        acc.x += x4.x; acc.y += x4.y; acc.z += x4.z; acc.w += x4.w;
+      }
+      stage_out[(j + 0) * kTileN + r] = finish(c_lo + j + 0, acc.x);
+      stage_out[(j + 1) * kTileN + r] = finish(c_lo + j + 1, acc.y);
+      stage_out[(j + 2) * kTileN + r] = finish(c_lo + j + 2, acc.z);
+      stage_out[(j + 3) * kTileN + r] = finish(c_lo + j + 3, acc.w);
+    }
+    __syncthreads();
+  }
+  // ---- 16-byte stores: 16 chunks of 8 features per column.  Section
+  // boundaries (q | k | v) are multiples of 64 features, so a chunk never
+  // straddles one.
+  for (int q = threadIdx.x; q < n_c * 16; q += kClusterThreads) {
+    const int cl = q >> 4, f0 = n0 + (q & 15) * 8;
+    const int b = m0 + c_lo + cl;
+    if (b >= a.M || f0 >= a.n_out) continue;
+    const uint4 val = *reinterpret_cast<const uint4*>(stage_out + (size_t)cl * kTileN + (q & 15) * 8);
+    T* dst;
+    if (f0 < qd) {
+      dst = static_cast<T*>(a.q_out) + (size_t)b * qd + f0;
+    } else {
+      const int slot = slot_of[c_lo + cl];
+      if (slot < 0) continue;
+      const bool is_k = f0 < qd + kd;
+      dst = static_cast<T*>(is_k ? a.k_cache : a.v_cache) + (size_t)slot * kd + (f0 - (is_k ? qd : qd + kd));
+    }
+    __stcs(reinterpret_cast<uint4*>(dst), val);
+  }
+  if (warp == 0) {
+    tc_fence_after();
+    const uint32_t ncols = BT <= 32 ? 32u : BT <= 64 ? 64u : BT <= 128 ? 128u : 256u;
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  }
+}
+
 }  // namespace
 
 }  // namespace clove
 
 using namespace clove;
+
+// Clusters of `splits` CTAs of this kernel that fit on the GPU at once,
+// cached per (device, dtype, splits, shared memory).
+template <typename Kern>
+static int resident_clusters(Kern kern, const cudaLaunchConfig_t& cfg, int device, int dtype, int splits,
+                             size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, size_t>, int> cache;
+  const auto key = std::make_tuple(device, dtype, splits, smem);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = n;
+  return n;
+}
 
 // Encode a 2-D K-major operand map {hidden, rows} with a 64 x box_rows box and
 // the 128-byte swizzle.
@@ -500,7 +780,8 @@ static QkvPlan plan_qkv(const clove_pool& pool, int batch, int hidden, int num_q
   P.smem = stage * P.nstage + staging + 1024;
   const size_t tiles = (size_t)P.ntiles_n * P.n_btiles;
   P.off_partials = (tiles * 4 + 255) & ~size_t(255);
-  P.ws_bytes = P.off_partials + tiles * P.max_contrib * P.batch_tile * kTileN * 4;
+  P.ws_bytes = P.batch_tile <= kStreamKMaxTile ? P.off_partials + tiles * P.max_contrib * P.batch_tile * kTileN * 4
+                                                : 256;  // the cluster schedule needs no workspace
   return P;
 }
 
@@ -611,11 +892,55 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x, const void* w_packed
   int prev = -1;
   cudaGetDevice(&prev);
   if (prev != pool->device) cudaSetDevice(pool->device);
-  auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_append_kernel<__nv_bfloat16> : qkv_append_kernel<__half>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem);
-  if (e == cudaSuccess)
-    kern<<<P.grid, kQkvThreads, P.smem, static_cast<cudaStream_t>(stream)>>>(tm_x, a);
-  if (e == cudaSuccess) e = cudaGetLastError();
+  cudaError_t e = cudaSuccess;
+  if (P.batch_tile <= kStreamKMaxTile) {
+    auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_append_kernel<__nv_bfloat16> : qkv_append_kernel<__half>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem);
+    if (e == cudaSuccess)
+      kern<<<P.grid, kQkvThreads, P.smem, static_cast<cudaStream_t>(stream)>>>(tm_x, a);
+    if (e == cudaSuccess) e = cudaGetLastError();
+  } else {
+    auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_cluster_kernel<__nv_bfloat16> : qkv_cluster_kernel<__half>;
+    const int ntiles = P.ntiles_n;
+    const size_t stage = (size_t)kTileN * 128 + (size_t)P.batch_tile * 128;
+    a.nstage = (int)std::min<size_t>(16, kRingBudget / stage);
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kClusterThreads);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // K splits: enough CTAs to cover the SMs, at most 8 (portable cluster),
+    // at least 2 K blocks each, and few enough clusters to be resident at
+    // once (a second wave would double the time)
+    int splits = std::max(1, std::min({pool->num_sms / (ntiles * P.n_btiles), 8, std::max(1, P.kb_total / 2)}));
+    size_t smem = 0;
+    for (; splits >= 1; --splits) {
+      // the epilogue's buffers overlay the ring and must fit in it: the
+      // receive buffer [splits][128][cs + 4] f32 (cs the columns per CTA
+      // rounded up to 16) and the output staging [cs][128]
+      const size_t cs = (((size_t)P.batch_tile + splits - 1) / splits + 15) & ~size_t(15);
+      const size_t recv = splits > 1 ? (size_t)splits * kTileN * (cs + 4) * 4 : 0;
+      if (recv + cs * kTileN * 2 > stage * a.nstage) continue;
+      smem = stage * a.nstage + 1024;
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess || splits == 1) break;
+      cfg.gridDim = dim3(ntiles, splits, P.n_btiles);
+      cfg.dynamicSmemBytes = smem;
+      attr[0].val.clusterDim.y = splits;
+      if (resident_clusters(kern, cfg, pool->device, (int)pool->dtype, splits, smem) >= ntiles * P.n_btiles) break;
+    }
+    a.splits = splits;
+    if (e == cudaSuccess) {
+      cfg.gridDim = dim3(ntiles, splits, P.n_btiles);
+      cfg.dynamicSmemBytes = smem;
+      attr[0].val.clusterDim.y = splits;
+      e = cudaLaunchKernelEx(&cfg, kern, tm_x, a);
+    }
+  }
   if (prev >= 0 && prev != pool->device) cudaSetDevice(prev);
   if (e != cudaSuccess) {
     set_last_error("qkv_append launch: %s", cudaGetErrorString(e));

@@ -97,21 +97,27 @@ def test_qkv_append_without_bias():
     _run(torch.bfloat16, 16, 256, 4, 2, 128, 16, 0.0, with_bias=False, seed=3)
 
 
-def test_qkv_append_flags_bad_slots_and_rejects_f32():
+@pytest.mark.parametrize("pad", [0, 38])  # batch 2 (stream-K schedule) and 40 (cluster schedule)
+def test_qkv_append_flags_bad_slots_and_rejects_f32(pad):
     from clove_b200 import KVPool, _lib
     dev = torch.device("cuda", 0)
-    pool = KVPool(8, 16, 2, 64, torch.bfloat16, 0)
+    pool = KVPool(8 + pad, 16, 2, 64, torch.bfloat16, 0)
     pool.storage.zero_()
     n_out = (4 + 4) * 64
-    x = torch.randn((2, 128), device=dev).to(torch.bfloat16)
+    B = 2 + pad
+    x = torch.randn((B, 128), device=dev).to(torch.bfloat16)
     w = torch.randn((n_out, 128), device=dev).to(torch.bfloat16)
-    bt = torch.tensor([[0, 1], [99, 2]], dtype=torch.int32, device=dev)  # seq 1: block id out of range
-    ctx = torch.tensor([40, 3], dtype=torch.int32, device=dev)           # seq 0: position past its table
+    # seq 0: position past its table; seq 1: block id out of range; the rest valid
+    bt = torch.tensor([[0, 1], [99, 2]] + [[8 + i, 0] for i in range(pad)], dtype=torch.int32, device=dev)
+    ctx = torch.tensor([40, 3] + [5] * pad, dtype=torch.int32, device=dev)
     pool.qkv_append(x, pool.pack_qkv_weights(w), None, 4, bt, ctx)
     torch.cuda.synchronize()
     st = pool.pool_status()
     assert st & _lib.FLAG_CTX_RANGE and st & _lib.FLAG_BLOCK_OOB
-    assert int(pool.storage.view(torch.int16).abs().sum()) == 0  # nothing written
+    written = pool.storage.view(torch.int16).reshape(2, -1, 16, 2 * 64).abs().sum(dim=(0, 3))  # [blocks, slots]
+    assert int(written[:8].sum()) == 0  # the two bad rows wrote nothing
+    if pad:
+        assert bool((written[8:, 5] != 0).all())  # every valid row wrote its slot
     p32 = KVPool(8, 16, 2, 64, torch.float32, 0)
     with pytest.raises(_lib.CloveError):
         p32.pack_qkv_weights(w.float())
