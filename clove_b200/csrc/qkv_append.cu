@@ -14,30 +14,38 @@
 // is small and the weights W [hidden, (Hq + 2 Hkv) D] are large: the kernel
 // streams the weights once, so HBM bandwidth bounds it.  The product is
 // computed transposed, D^T = W^T x^T: the 128-row tensor-core tile runs over
-// output features and the batch is the MMA's N dimension (16..256).  Both
-// operands are K-major in shared memory with the 128-byte swizzle: W^T is
-// stored [N_out, hidden] (rows of the reference's W laid out contiguously
-// along hidden), x is [M, hidden].
+// output features and the batch is the MMA's N dimension (16..256).
 //
-// Schedule (stream-K).  The work is (feature tile of 128) x (batch tile) x
-// (64-wide K block) units, split evenly and contiguously over one CTA per SM,
-// so every SM streams weights for the whole kernel whatever the tile count.
-// A CTA's range covers pieces ("segments") of one or more tiles.  A segment
-// that is a whole tile goes straight to the epilogue; otherwise its f32
-// partial goes to a workspace slot, and the CTA that completes the tile's
-// last piece (a per-tile arrival counter, reset by that CTA) sums the
-// partials in slot order and runs the epilogue.
+// Weight layout.  W^T is packed once (clove_cuda_qkv_pack_weights) into
+// 128-feature x 64-element tiles, each a contiguous 16 KB chunk already in the
+// 128-byte-swizzled K-major order the tensor cores read, so one (feature
+// tile, K block) is one plain bulk copy and a CTA streams consecutive chunks
+// (row-strided tensor-map boxes cost DRAM page locality once every SM
+// streams).  x, small and L2-resident, comes through a 2-D tensor map with
+// the same swizzle.
 //
-// Roles in a CTA (192 threads): warp 0 lane 0 issues the bulk-tensor copies
-// (TMA) into a ring of stages; warp 1 lane 0 issues tcgen05.mma into one of
-// two tensor-memory accumulators (so one segment drains while the next
-// accumulates) and commits stages back to the producer; warps 2-5 (tensor-
-// memory lane groups 2, 3, 0, 1: one output feature per thread) drain
-// accumulators, add the bias, rotate, round, stage a tile's columns in shared
-// memory and write each column's 128 features — contiguous in q's row or in
-// the cache slot row — as 16-byte stores.  Every wait is bounded; a wait that
-// runs out sets CLOVE_FLAG_TIMEOUT in the pool's flag word and the CTA
-// finishes without hanging.
+// Two schedules, by batch tile:
+//  - up to 32 columns, stream-K (qkv_append_kernel): (feature tile) x (batch
+//    tile) x (64-wide K block) units split evenly and contiguously over one
+//    CTA per SM, so every SM streams whatever the tile count.  A CTA's range
+//    covers pieces ("segments") of one or more tiles.  A whole-tile segment
+//    goes straight to the epilogue; otherwise its f32 partial goes to a
+//    workspace slot, and the CTA that completes the tile's last piece (a
+//    per-tile arrival counter, reset by that CTA) sums the partials in slot
+//    order and runs the epilogue.  192 threads: warp 0 lane 0 issues the
+//    copies into a ring of stages; warp 1 lane 0 issues tcgen05.mma into one
+//    of two tensor-memory accumulators (one segment drains while the next
+//    accumulates) and commits stages back; warps 2-5 (tensor-memory lane
+//    groups 2, 3, 0, 1: one output feature per thread) run the epilogue.
+//  - larger tiles, a cluster schedule (qkv_cluster_kernel): the K splits of
+//    a feature tile form a thread-block cluster and reduce through
+//    distributed shared memory, each CTA finishing a slice of the columns —
+//    at large tiles the partials are too big for one CTA to sum.
+// The epilogue adds the bias, rotates, rounds, stages a tile's columns in
+// shared memory and writes each column's 128 features — contiguous in q's
+// row or in the cache slot row — as 16-byte stores.  Every wait is bounded;
+// a wait that runs out sets CLOVE_FLAG_TIMEOUT in the pool's flag word and
+// the CTA finishes without hanging.
 #include <algorithm>
 #include <cmath>
 #include <map>
