@@ -25,7 +25,8 @@
 // the same swizzle.
 //
 // Two schedules, by batch tile:
-//  - up to 32 columns, stream-K (qkv_append_kernel): (feature tile) x (batch
+//  - up to 32 columns (64 when clusters would leave SMs idle), stream-K
+//    (qkv_append_kernel): (feature tile) x (batch
 //    tile) x (64-wide K block) units split evenly and contiguously over one
 //    CTA per SM, so every SM streams whatever the tile count.  A CTA's range
 //    covers pieces ("segments") of one or more tiles.  A whole-tile segment
@@ -64,7 +65,7 @@ namespace {
 constexpr int kQkvThreads = 192;  // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
 constexpr int kEpiThreads = 128;
 constexpr int kClusterThreads = 256;  // cluster schedule: warp 0 copies, warp 1 MMAs, all 8 in the epilogue
-constexpr int kStreamKMaxTile = 32;   // batch tiles up to this use stream-K, larger ones the cluster schedule
+constexpr int kStreamKMaxTile = 32;   // batch tiles up to this always use stream-K (see plan_qkv)
 constexpr size_t kRingBudget = 200 * 1024;  // cluster schedule: ring bytes (its epilogue buffers overlay it)
 constexpr int kTileN = 128;       // output features per tile (tensor-core M)
 constexpr int kTileK = 64;        // hidden elements per stage (one 128-byte swizzle row)
@@ -764,6 +765,7 @@ static size_t packed_bytes(int n_out, int hidden) {
 
 // Schedule and workspace of one call.
 struct QkvPlan {
+  bool stream_k;  // false: the cluster schedule
   int batch_tile, ntiles_n, n_btiles, kb_total, grid, max_contrib, nstage, acc_cols;
   long long units;
   size_t smem, off_partials, ws_bytes;
@@ -777,6 +779,13 @@ static QkvPlan plan_qkv(const clove_pool& pool, int batch, int hidden, int num_q
   P.ntiles_n = (n_out + kTileN - 1) / kTileN;
   P.kb_total = (hidden + kTileK - 1) / kTileK;
   P.units = (long long)P.ntiles_n * P.n_btiles * P.kb_total;
+  // Stream-K for small batch tiles (partials are cheap to sum), and for
+  // tiles up to 64 columns when the cluster grid (feature tiles x K splits)
+  // would leave over 40 % of the SMs idle; clusters otherwise.
+  const int tiles_mn = P.ntiles_n * P.n_btiles;
+  const int splits_hint = std::max(1, std::min({pool.num_sms / tiles_mn, 8, std::max(1, P.kb_total / 2)}));
+  P.stream_k = P.batch_tile <= kStreamKMaxTile ||
+               (P.batch_tile <= 2 * kStreamKMaxTile && 10 * tiles_mn * splits_hint < 6 * pool.num_sms);
   // one CTA per SM, at least two K blocks each
   P.grid = (int)std::max(1LL, std::min((long long)pool.num_sms, P.units / 2));
   const long long per_cta = P.units / P.grid;  // shortest range
@@ -788,7 +797,7 @@ static QkvPlan plan_qkv(const clove_pool& pool, int batch, int hidden, int num_q
   P.smem = stage * P.nstage + staging + 1024;
   const size_t tiles = (size_t)P.ntiles_n * P.n_btiles;
   P.off_partials = (tiles * 4 + 255) & ~size_t(255);
-  P.ws_bytes = P.batch_tile <= kStreamKMaxTile ? P.off_partials + tiles * P.max_contrib * P.batch_tile * kTileN * 4
+  P.ws_bytes = P.stream_k ? P.off_partials + tiles * P.max_contrib * P.batch_tile * kTileN * 4
                                                 : 256;  // the cluster schedule needs no workspace
   return P;
 }
@@ -901,7 +910,7 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x, const void* w_packed
   cudaGetDevice(&prev);
   if (prev != pool->device) cudaSetDevice(pool->device);
   cudaError_t e = cudaSuccess;
-  if (P.batch_tile <= kStreamKMaxTile) {
+  if (P.stream_k) {
     auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_append_kernel<__nv_bfloat16> : qkv_append_kernel<__half>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem);
     if (e == cudaSuccess)
