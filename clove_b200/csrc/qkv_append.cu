@@ -96,6 +96,7 @@ struct QkvArgs {
   long long units;  // tiles * kb_total
   float rope_theta;
   uint32_t wait_limit;
+  int inject_stall;  // test hook: the first stage of the first CTA is never filled
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
@@ -252,6 +253,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       // producer: W^T tile [128 features, 64] and x tile [BT, 64] per stage
       int i = 0;
       bool ok = true;
+      const bool stall = a.inject_stall && blockIdx.x == 0;
       for (long long u = u_begin; u < u_end && ok;) {
         const Segment sg = segment_at(u, u_end, a.kb_total);
         u += sg.kb1 - sg.kb0;
@@ -263,6 +265,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
             ok = false;
             break;
           }
+          if (stall && i == 0) continue;  // test hook: stage 0 never filled
           unsigned char* st = smem + (size_t)s * stage_bytes;
           mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
           const int k0 = kb * kTileK;  // 64 elements = 128 bytes: meets the 16-byte rule
@@ -275,7 +278,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         }
       }
       // drain: the last copies must land before the CTA exits
-      for (int t = max(0, i - a.nstage); t < i; ++t)
+      for (int t = max(stall ? 1 : 0, i - a.nstage); t < i; ++t)
         mbar_wait_bounded(&full_bar[t % a.nstage], (uint32_t)(t / a.nstage) & 1u, a.flags, a.wait_limit);
     }
     __syncwarp();
@@ -321,9 +324,24 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const int qd = a.hq * a.D, kd = a.hkv * a.D;
     int j = 0;
+    bool aborted = false;
     for (long long u = u_begin; u < u_end; ++j) {
       const Segment sg = segment_at(u, u_end, a.kb_total);
       u += sg.kb1 - sg.kb0;
+      const bool whole = sg.kb0 == 0 && sg.kb1 == a.kb_total;
+      const long long t0 = (long long)sg.tile * a.kb_total;
+      const int g_first = first_cta(t0, a.units, G);
+      const int n_contrib = first_cta(t0 + a.kb_total - 1, a.units, G) - g_first + 1;
+      if (!aborted) {
+        const bool ok = mbar_wait_bounded(&acc_full[(j & 1)], (uint32_t)(j >> 1) & 1u, a.flags, a.wait_limit);
+        aborted = named_bar_or(1, kEpiThreads, !ok);  // every epilogue warp decides together
+      }
+      if (aborted) {
+        // the flag is set; still count this CTA's pieces so that every tile's
+        // arrival counter returns to zero and the workspace stays usable
+        if (!whole && e == 0 && atomicAdd(a.counters + sg.tile, 1) == n_contrib - 1) a.counters[sg.tile] = 0;
+        continue;
+      }
       const int tile_n = sg.tile % a.ntiles_n, m0 = (sg.tile / a.ntiles_n) * kMaxBatchTile;
       const int n0 = tile_n * kTileN;
       const int f = n0 + r;
@@ -348,9 +366,6 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       };
 
       const int buf = j & 1;
-      const uint32_t use = (uint32_t)(j >> 1);
-      const bool ok = mbar_wait_bounded(&acc_full[buf], use & 1u, a.flags, a.wait_limit);
-      if (named_bar_or(1, kEpiThreads, !ok)) break;  // every epilogue warp leaves together
       tc_fence_after();
       // cache slot of each column, once per tile (read by the stores below,
       // after the staging barrier)
@@ -371,7 +386,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         slot_of[c] = slot;
       }
       const uint32_t acc = tmem + lane_off + (uint32_t)(buf * a.acc_cols);
-      if (sg.kb0 == 0 && sg.kb1 == a.kb_total) {
+      if (whole) {
         // the whole tile in this CTA
         for (int c0 = 0; c0 < BT; c0 += 16) {
           float v[16];
@@ -383,9 +398,6 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         mbar_arrive(&acc_empty[buf]);
       } else {
         // a piece: publish the partial in this CTA's slot of the tile
-        const long long t0 = (long long)sg.tile * a.kb_total;
-        const int g_first = first_cta(t0, a.units, G);
-        const int n_contrib = first_cta(t0 + a.kb_total - 1, a.units, G) - g_first + 1;
         float* part = a.partials + (size_t)sg.tile * a.max_contrib * BT * kTileN;
         float* mine = part + (size_t)(blockIdx.x - g_first) * BT * kTileN;
         // feature-major [slot][feature][column]: each thread moves its own
@@ -520,10 +532,15 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
     if (lane == 0) {
       // producer: W^T tile [128 features, 64] and x tile [BT, 64] per stage
       int issued = 0;
+      const bool stall = a.inject_stall && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
       for (int i = 0; i < nkb; ++i) {
         const int s = i % a.nstage;
         const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
         if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1u, a.flags, a.wait_limit)) break;
+        if (stall && i == 0) {  // test hook: stage 0 never filled
+          ++issued;
+          continue;
+        }
         unsigned char* st = smem + (size_t)s * stage_bytes;
         mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
         const int k0 = (kb0 + i) * kTileK;  // 64 elements = 128 bytes: meets the 16-byte rule
@@ -534,7 +551,7 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
         ++issued;
       }
       // drain: the copies issued last must have landed before shared memory is reused
-      for (int i = max(0, issued - a.nstage); i < issued; ++i)
+      for (int i = max(stall ? 1 : 0, issued - a.nstage); i < issued; ++i)
         mbar_wait_bounded(&full_bar[i % a.nstage], (uint32_t)(i / a.nstage) & 1u, a.flags, a.wait_limit);
     }
     __syncwarp();
@@ -898,6 +915,7 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x, const void* w_packed
   a.acc_cols = P.acc_cols;
   a.units = P.units;
   a.rope_theta = rope_theta;
+  a.inject_stall = debug_inject_stall();
   const uint32_t lim = debug_wait_limit();
   a.wait_limit = lim ? lim : kWaitLimit;
 

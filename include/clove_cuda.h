@@ -215,8 +215,9 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k,
  * skipped and flagged in the pool's status word, like
  * clove_cuda_reshape_and_cache.  Scratch: clove_cuda_qkv_workspace_size
  * bytes, 256-byte aligned, ZERO-FILLED before its first use; every call
- * that completes leaves it zeroed again (its per-tile counters), so one
- * buffer serves all later calls on a stream.  f32 pools return
+ * leaves it zeroed again (its per-tile counters), including one whose
+ * bounded waits ran out (CLOVE_FLAG_TIMEOUT in the pool's status word), so
+ * one buffer serves all later calls on a stream.  f32 pools return
  * CLOVE_ERR_UNSUPPORTED. */
 size_t clove_cuda_qkv_packed_bytes(int n_out, int hidden);
 int clove_cuda_qkv_pack_weights(int dtype, const void* w_t, int n_out,

@@ -157,3 +157,43 @@ def test_fused_module_forward_matches_unfused(theta):
     ref = oracle.linear(attn.reshape(B, -1), m.w_o.weight.double().cpu().numpy(), m.w_o.bias.double().cpu().numpy())
     ok, worst = oracle.tolerance_ok(out.double().cpu().numpy(), ref, 2e-2)
     assert ok, worst
+
+
+@pytest.mark.parametrize("B", [5, 128])  # stream-K and cluster schedules
+def test_stuck_wait_times_out_and_next_call_is_correct(B):
+    # Failure detection without a GPU fault: the test hook leaves the first
+    # stage of the first CTA unfilled, so the bounded waits run out; the call
+    # must finish and report CLOVE_FLAG_TIMEOUT, the workspace counters must
+    # be zero again, and the next call on the same pool and workspace must be
+    # right.
+    import time
+
+    from clove_b200 import KVPool, _lib
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    hidden, hq, hkv, D, bs = 1024, 8, 2, 128, 16
+    n_out = (hq + 2 * hkv) * D
+    pool = KVPool(B + 4, bs, hkv, D, torch.bfloat16, 0)
+    x = torch.randn((B, hidden), device=dev).to(torch.bfloat16)
+    w = (torch.randn((n_out, hidden), device=dev) / 32).to(torch.bfloat16)
+    wp = pool.pack_qkv_weights(w)
+    bt = torch.arange(B, dtype=torch.int32, device=dev).reshape(B, 1)
+    ctx = torch.full((B,), 3, dtype=torch.int32, device=dev)
+    try:
+        _lib.check(L.clove_cuda_debug_set(2000, 1))
+        t0 = time.time()
+        pool.qkv_append(x, wp, None, hq, bt, ctx)
+        flags = pool.pool_status()
+        elapsed = time.time() - t0
+    finally:
+        L.clove_cuda_debug_set(0, 0)
+    assert flags & _lib.FLAG_TIMEOUT, flags
+    assert elapsed < 30
+    tiles = -(-n_out // 128)
+    assert int(pool._qkv_ws[:4 * tiles].view(torch.int32).abs().sum()) == 0
+    q, _ = pool.qkv_append(x, wp, None, hq, bt, ctx)
+    torch.cuda.synchronize()
+    assert pool.pool_status() == 0
+    ref = (x.double() @ w.double().t())[:, :hq * D]
+    got = q.double().reshape(B, -1)
+    assert bool(((got - ref).abs() <= 2.0 ** -8 * ref.abs() * 1.0001 + 2e-4 * ref.pow(2).mean().sqrt()).all())
