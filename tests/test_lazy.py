@@ -59,3 +59,28 @@ def test_unused_nodes_are_not_planned():
     lb, out = _trace((4, 128), (2, 64, 16, 2, 64))
     lb.matmul(lb.input("a", (4, 4)), lb.input("b", (4, 4)))  # dead branch
     assert [s.op for s in compile(lb.graph, [out])] == [Opcode.PAGED_ATTENTION]
+
+
+def test_execute_binds_symbols_and_runs_linear_steps_on_any_device():
+    # host logic of execute(): symbolic dims bind from the feeds, a mismatch
+    # raises, and a Linear step is one addmm (bit-equal to torch.addmm)
+    import torch
+
+    from clove_b200.lazy import execute
+    lb = LazyBackend()
+    x = lb.input("x", ("B", 8))
+    w, b = lb.input("w", (8, 4)), lb.input("b", (4,))
+    y = lb.add(lb.matmul(x, w), b)
+    steps = compile(lb.graph, [y])
+    assert [s.op for s in steps] == [Opcode.LINEAR]
+    g = torch.Generator().manual_seed(0)
+    feeds = {"x": torch.randn(3, 8, generator=g), "w": torch.randn(8, 4, generator=g), "b": torch.randn(4, generator=g)}
+    out = execute(lb.graph, steps, feeds)[y.id]
+    assert torch.equal(out, torch.addmm(feeds["b"], feeds["x"], feeds["w"]))
+    with pytest.raises(ValueError, match="dimension"):
+        execute(lb.graph, steps, {**feeds, "w": torch.randn(9, 4)})
+    lb2 = LazyBackend()
+    a1, a2 = lb2.input("a1", ("B", 4)), lb2.input("a2", ("B", 4))
+    s2 = lb2.add(a1, a2)
+    with pytest.raises(ValueError, match="symbol B"):
+        execute(lb2.graph, compile(lb2.graph, [s2]), {"a1": torch.zeros(2, 4), "a2": torch.zeros(3, 4)})
