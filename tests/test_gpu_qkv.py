@@ -88,6 +88,8 @@ def _run(dtype, B, hidden, hq, hkv, D, bs, theta, with_bias=True, seed=0):
     (300, 1024, 16, 4, 128, 32, 0.0),      # two batch tiles
     (33, 520, 4, 4, 64, 8, 10000.0),       # hidden not a multiple of 64 (zero-filled tail)
     (64, 8192, 64, 8, 128, 16, 0.0),       # 70B-shaped projection
+    (7, 384, 3, 1, 64, 16, 10000.0),       # 320 features: a partial last tile, q/k boundary mid-tile
+    (40, 384, 3, 1, 64, 16, 10000.0),      # the same through the cluster schedule
 ])
 def test_qkv_append_matches_oracle(dtype, B, hidden, hq, hkv, D, bs, theta):
     _run(dtype, B, hidden, hq, hkv, D, bs, theta, seed=B + hidden)
