@@ -18,7 +18,10 @@ hold symbols (the reference's SymInt): a str dimension is bound at execute()
 from the fed tensors.
 
 MatMul / Add (the projections of PagedAttention::forward, src/nn.rs:538-545)
-run as torch GPU ops: they are off the path and not part of its kernels.
+run as torch ops: they are off the path and not part of its kernels.  The
+planner fuses a MatMul whose only consumer adds a bias row into one Linear
+step (one GEMM with the bias in its epilogue, as the eager Linear runs it),
+so a compiled graph reproduces the eager module bit for bit.
 """
 from __future__ import annotations
 
