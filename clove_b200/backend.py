@@ -19,6 +19,7 @@ Errors raise CloveError (the reference panics, src/backend.rs:2937-2948).
 from __future__ import annotations
 
 import math
+from collections import OrderedDict
 
 import torch
 
@@ -26,9 +27,13 @@ from .ops import KVPool
 
 
 class CudaBackend:
-    """Stateless apart from a cache of pool handles keyed by kv_cache storage."""
+    """Stateless apart from a bounded cache of pool handles keyed by kv_cache
+    storage.  A cached pool keeps its kv_cache alive, so the cache holds the
+    most recently used MAX_POOLS caches only; an evicted one is wrapped again
+    (tensor maps re-encoded) on its next use."""
 
-    _pools: dict[tuple[int, tuple, torch.dtype], KVPool] = {}
+    MAX_POOLS = 64
+    _pools: OrderedDict[tuple[int, tuple, torch.dtype], KVPool] = OrderedDict()
 
     @classmethod
     def _pool(cls, kv_cache: torch.Tensor) -> KVPool:
@@ -40,6 +45,9 @@ class CudaBackend:
             _, nb, bs, hkv, d = kv_cache.shape
             pool = KVPool(nb, bs, hkv, d, dtype=kv_cache.dtype, device=kv_cache.device, storage=kv_cache)
             cls._pools[key] = pool
+            while len(cls._pools) > cls.MAX_POOLS:
+                cls._pools.popitem(last=False)  # the handle closes once nothing else holds the pool
+        cls._pools.move_to_end(key)
         return pool
 
     @classmethod
