@@ -76,8 +76,19 @@ void* cache_alloc(int device, size_t cap) {
     }
   }
   void* p = nullptr;
-  if (cudaMalloc(&p, cap) != cudaSuccess) return nullptr;
-  return p;
+  if (cudaMalloc(&p, cap) == cudaSuccess) return p;
+  // out of memory with buffers parked in the cache: give them back and retry once
+  cudaGetLastError();
+  {
+    std::lock_guard<std::mutex> lk(c.mu);
+    for (auto& kv : c.free_lists)
+      for (void* q : kv.second) cudaFree(q);
+    c.free_lists.clear();
+    c.held = 0;
+  }
+  if (cudaMalloc(&p, cap) == cudaSuccess) return p;
+  cudaGetLastError();
+  return nullptr;
 }
 
 void cache_release(int device, void* p, size_t cap) {
