@@ -3,10 +3,15 @@
 One step = append one token per sequence through the slot mapping, then decode
 every sequence over ctx+1 tokens (one call of the fused C-ABI entry point).
 Default workload: configuration c2 (Llama-7B-shaped, f32 KV, batch 64, 32
-heads x 128, block 16, context 2048, 16384-block pool).  Under torchrun each
-rank runs its own full c2 workload (weak scaling; sequences are independent,
-no data-path collective).  Inputs (4.3 GB of KV per rank) exceed the 126 MB
-L2, so no flush is needed between steps.
+heads x 128, block 16, context 2048, 16384-block pool).  Under torchrun the
+64 sequences shard over the N GPUs with distribute_batch's contiguous split
+(strong scaling: each GPU owns its sequences' blocks in its own pool; no
+data-path collective).  `--weak` gives every rank a full replica instead.
+After the headline, configurations c3, c4, c5 are measured at the same N in
+the same run (`per_config`): c3/c5 sharded by attended tokens, c4 split by
+KV heads with one NCCL all-gather of the outputs on N > 1.  Inputs exceed
+the 126 MB L2 (c2 4.3 GB of KV per step), so no flush is needed between
+steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2]
   python bench.py --impl reference ...   # CPU arm (the oracle port)
@@ -27,10 +32,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "paged-attn decode tokens/s"
 
-# DRAM bytes (read + write) per decode launch on rank 0's default workload,
-# from the ncu captures summarised in profiles/ (paged_decode_simt_c2.md,
-# paged_decode_mma_c3_c4.md).  Reported as roofline.traffic next to the
-# algorithmic bytes; None where no full-size capture exists.
+# DRAM bytes (read + write) per decode launch of the 1-GPU workload, from
+# earlier full-size ncu captures of the decode kernel (the committed profile
+# summaries).  Reported as roofline.traffic next to the algorithmic bytes;
+# None where no full-size capture exists.
 TRAFFIC_MEASURED = {"c2": 4334.7e6, "c3": 694.3e6}
 
 
@@ -87,20 +92,53 @@ class ClockSampler:
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def host_sample_case(spec, n_seqs: int, seed: int = 1):
+def host_sample_case(spec, n_seqs: int, seed: int = 1, with_append: bool = False):
     """A CPU-side case with the shapes and value distributions of `spec` for
-    `n_seqs` sequences (a pool of exactly the blocks they use)."""
+    `n_seqs` sequences (a pool of exactly the blocks they use), drawn with
+    numpy on the host (timing input only; nothing is compared).  Returns
+    (layout, (k_cache, v_cache, block_tables, ctx + 1, q[, k_new, v_new,
+    slots])) as numpy arrays (16-bit types as bit patterns)."""
     import numpy as np
     from dataclasses import replace
 
     import torch
 
-    from clove_b200.workload import fill_values, make_layout, to_numpy_bits
+    import oracle
+    from clove_b200.workload import make_layout
     lay = make_layout(replace(spec, num_blocks=0, tables="permutation"), seed=spec.seed + seed, batch=n_seqs)
-    q, _, _, st = fill_values(lay, "cpu")
-    bits = to_numpy_bits(st)
-    return lay, (np.ascontiguousarray(bits[0]), np.ascontiguousarray(bits[1]), lay.block_tables,
-                 (lay.context_lens + 1).astype(np.int32), to_numpy_bits(q))
+    rng = np.random.default_rng(spec.seed + seed)
+    f32 = spec.dtype == torch.float32
+    # one 16 Mi-element block of N(0,1) draws, tiled (CPU timing input only;
+    # drawing every element costs more than the timed steps on large pools)
+    src = rng.standard_normal(1 << 24, dtype=np.float32)
+
+    def draw(shape, scale=1.0):
+        x = np.empty(shape, np.float32)
+        flat = x.reshape(-1)
+        step = src.size
+        for i in range(0, flat.size, step):
+            n = min(step, flat.size - i)
+            flat[i:i + n] = src[:n]
+        if scale != 1.0:
+            x *= np.float32(scale)
+        if f32:
+            return x
+        if spec.dtype == torch.float16:
+            return x.astype(np.float16).view(np.uint16)
+        u = x.view(np.uint32)  # bf16, round to nearest even
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+    row = (spec.block_size, spec.num_kv_heads, spec.head_dim)
+    kc = draw((lay.num_blocks,) + row, spec.kv_scale)
+    vc = draw((lay.num_blocks,) + row, spec.kv_scale)
+    q = draw((lay.batch, spec.num_q_heads, spec.head_dim))
+    case = (kc, vc, lay.block_tables, (lay.context_lens + 1).astype(np.int32), q)
+    if with_append:
+        slots = oracle.append_slots(lay.block_tables, lay.context_lens, spec.block_size)
+        kn = draw((lay.batch, spec.num_kv_heads, spec.head_dim), spec.kv_scale)
+        vn = draw((lay.batch, spec.num_kv_heads, spec.head_dim), spec.kv_scale)
+        case = case + (kn, vn, slots)
+    return lay, case
 
 
 def cpu_arm(lay, case, budget_s: float, max_reps: int | None = None) -> dict:
@@ -140,32 +178,88 @@ def _dist():
 
 
 def run_reference(args) -> None:
-    """CPU arm: the oracle port of the reference's CPU idiom on the host cores,
-    a bounded sample of the workload per step; rank 0 only."""
+    """CPU arm: the oracle port of the reference's CPU idiom (slot-mapping
+    append + f32 decode) on all host cores, rank 0 only.  A step is the
+    configured workload's whole batch when (steps + warmup) such steps fit
+    in about 150 s, else the first n sequences of it (n >= 8)."""
+    import numpy as np
+
+    import oracle
+    from clove_b200.workload import CONFIGS, dtype_code
+
     ws, rank, _ = _dist()
     if rank != 0:
         return
-    from clove_b200.workload import CONFIGS
     spec = CONFIGS[args.config]
-    n = args.cpu_seqs
-    lay, case = host_sample_case(spec, n)
-    for _ in range(args.warmup):
-        cpu_arm(lay, case, 0.0, max_reps=1)
+    lay, case = host_sample_case(spec, spec.batch if args.batch is None else args.batch, with_append=True)
+    kc, vc, bt, ctx, qs, kn, vn, slots = case
+    threads = os.cpu_count() or 1
+    code = dtype_code(spec.dtype)
+    scale = 1.0 / np.sqrt(spec.head_dim)
+
+    def step(n):
+        oracle.reshape_and_cache(kc, vc, kn[:n], vn[:n], slots[:n])
+        oracle.decode_f32(code, qs[:n], kc, vc, bt[:n], ctx[:n], scale, nthreads=threads)
+
+    n = lay.batch
+    t0 = time.perf_counter()
+    step(n)
+    t1 = time.perf_counter() - t0
+    budget = 150.0
+    if (args.steps + args.warmup) * t1 > budget:
+        n = max(8, min(n, int(n * budget / ((args.steps + args.warmup) * t1))))
+    for _ in range(max(args.warmup - 1, 0)):
+        step(n)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu_arm(lay, case, 0.0, max_reps=1)
+        step(n)
     el = time.perf_counter() - t0
     val = n * args.steps / el
-    cb = {"value": val, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
-          "sample": f"per step {n} sequences shaped like config {spec.name} (ctx+1 = "
-                    f"{int(case[3].min())}..{int(case[3].max())}), oracle f32 restatement, all host threads"}
+    cb = {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
+          "sample": f"per step {n} of the {lay.batch} sequences of config {spec.name} (ctx+1 = "
+                    f"{int(ctx[:n].min())}..{int(ctx[:n].max())}): slot-mapping append + f32 decode, "
+                    f"oracle restatement of the reference's CPU idiom on {threads} host threads"}
     print(json.dumps({"metric": METRIC, "value": val, "unit": "tokens/s", "impl": "reference", "n_gpus": ws,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
-                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": _dtype_name(spec.dtype),
-                      "data": "synthetic", "config": {"workload": spec.name, "batch_per_step": n},
+                      "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                      "dtype": _dtype_name(spec.dtype), "data": "synthetic",
+                      "config": headline_config(args.config, ws, args.weak, args.batch),
                       "cpu_baseline": cb,
                       "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                               "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def _partition(mode: str, name: str, ws: int) -> str:
+    return {"heads": f"kv-heads/{ws} + NCCL all-gather of outputs",
+            "sequences": (f"sequences sharded over {ws} GPUs ({_policy(name)}), own pool per GPU, no collective")
+            if ws > 1 else "1 GPU",
+            "replica": f"{ws} independent full replicas"}[mode]
+
+
+def headline_config(name: str, ws: int, weak: bool, batch=None) -> dict:
+    """The `config` object of the headline line (both arms), from host-side
+    layout metadata only."""
+    from dataclasses import replace
+
+    from clove_b200.workload import CONFIGS, make_layout, shard_layout
+    spec = CONFIGS[name]
+    if batch is not None:
+        spec = replace(spec, num_blocks=0)
+    if name == "c4" and ws > 1:
+        mode, lay = "heads", make_layout(spec, batch=batch)
+        gb, kv = lay.batch, lay.kv_bytes()
+    elif weak and ws > 1:
+        mode, lay = "replica", make_layout(spec, batch=batch)
+        gb, kv = lay.batch * ws, lay.kv_bytes() * ws
+    else:
+        mode = "sequences"
+        lay, _ = shard_layout(spec, ws, 0, batch=batch)
+        gb, kv = lay.extra.get("global_batch", lay.batch), lay.extra.get("global_kv_bytes", lay.kv_bytes())
+    return {"workload": spec.name, "description": spec.description, "batch_per_gpu": lay.batch,
+            "global_batch": gb, "num_q_heads": spec.num_q_heads, "num_kv_heads": spec.num_kv_heads,
+            "head_dim": spec.head_dim, "block_size": spec.block_size, "num_blocks_per_gpu": lay.num_blocks,
+            "kv_bytes_per_step": kv, "l2": "inputs larger than L2 (no flush)",
+            "parallelism": _partition(mode, name, ws)}
 
 
 def _dtype_name(dt) -> str:
@@ -173,115 +267,234 @@ def _dtype_name(dt) -> str:
     return {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16"}[dt]
 
 
-def run_ours(args) -> None:
+class DecodeCase:
+    """One configuration's decode step on this rank: its pool, inputs and a
+    `step()` that launches append + decode (+ the output all-gather under KV
+    -head sharding) on the current stream."""
+
+    def __init__(self, name: str, ws: int, rank: int, dev, batch=None, weak: bool = False):
+        from dataclasses import replace
+
+        import torch
+
+        from clove_b200 import KVPool
+        from clove_b200.distributed import head_sharded_append_decode
+        from clove_b200.workload import CONFIGS, fill_values, make_layout, shard_layout
+
+        spec = CONFIGS[name]
+        if batch is not None:
+            spec = replace(spec, num_blocks=0)  # pool sized to the blocks used (profiling)
+        self.spec, self.ws, self.rank, self.dev = spec, ws, rank, dev
+        # c4 on N > 1 GPUs: KV heads split across ranks + one all-gather of
+        # the outputs.  Every other configuration on N > 1 GPUs: the global
+        # batch sharded by sequence (own pool and tables per rank, no
+        # collective); --weak gives every rank a full replica instead.
+        self.head_split = name == "c4" and ws > 1
+        self.mode = "heads" if self.head_split else ("replica" if weak and ws > 1 else "sequences")
+        if self.head_split:
+            lay = make_layout(spec, seed=spec.seed, batch=batch)  # same tables on every rank
+            lspec = replace(spec, num_kv_heads=spec.num_kv_heads // ws, num_q_heads=spec.num_q_heads // ws,
+                            seed=spec.seed + rank)
+            llay = replace(lay, spec=lspec, seed=lspec.seed)
+            self.pool = KVPool(lay.num_blocks, spec.block_size, lspec.num_kv_heads, spec.head_dim, spec.dtype, dev)
+            _, kn, vn, _ = fill_values(llay, dev, self.pool.storage)
+            gq = torch.Generator(device=dev)
+            gq.manual_seed(spec.seed)
+            q_all = torch.randn((lay.batch, spec.num_q_heads, spec.head_dim), generator=gq, device=dev).to(spec.dtype)
+            hl = spec.num_q_heads // ws
+            q = q_all[:, rank * hl:(rank + 1) * hl].contiguous()  # this rank's query heads
+            self.gbuf = torch.empty((ws * lay.batch, hl, spec.head_dim), dtype=torch.float32, device=dev)
+            self.global_batch = lay.batch
+            self.kv_local = lay.kv_bytes() // ws
+            self.kv_total = lay.kv_bytes()
+        else:
+            if self.mode == "replica":
+                lay = make_layout(spec, seed=spec.seed + rank, batch=batch)
+                self.global_batch = lay.batch * ws
+                self.kv_total = lay.kv_bytes() * ws
+            else:
+                lay, _ = shard_layout(spec, ws, rank, batch=batch)
+                self.global_batch = lay.extra.get("global_batch", lay.batch)
+                self.kv_total = lay.extra.get("global_kv_bytes", lay.kv_bytes())
+            self.kv_local = lay.kv_bytes()
+            self.pool = KVPool(lay.num_blocks, spec.block_size, spec.num_kv_heads, spec.head_dim, spec.dtype, dev)
+            q, kn, vn, _ = fill_values(lay, dev, self.pool.storage)
+        self.lay, self.q, self.kn, self.vn = lay, q, kn, vn
+        self.bt = torch.from_numpy(lay.block_tables).to(dev)
+        self.cl = torch.from_numpy(lay.context_lens).to(dev)
+        self.out = torch.empty((lay.batch, q.shape[1], spec.head_dim), dtype=torch.float32, device=dev)
+        self.max_ctx = lay.max_ctx
+        self._hs = head_sharded_append_decode
+
+    def decode(self):
+        return self.pool.append_decode(self.q, self.kn, self.vn, self.bt, self.cl, max_ctx=self.max_ctx, out=self.out)
+
+    def gather(self):
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(self.gbuf, self.out)
+
+    def step(self):
+        self.decode()
+        if self.head_split:
+            self.gather()
+
+    def close(self):
+        self.pool.close()
+
+
+def _max_over_ranks(x: float, ws: int, dev) -> float:
     import torch
     import torch.distributed as dist
+    if ws <= 1:
+        return x
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
-    from clove_b200 import KVPool, launch_count
-    from clove_b200.workload import CONFIGS, fill_values, make_layout
 
-    from dataclasses import replace
+def _barrier(ws: int) -> None:
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
 
-    from clove_b200.distributed import head_sharded_append_decode
+
+def time_case(case: DecodeCase, steps: int, warmup: int, graph: bool = True, local: int = 0):
+    """Warm up, capture one step in a CUDA graph, and time `steps` replays
+    with CUDA events (barrier + synchronize on both sides).  Returns
+    (ms per step on this rank, max over ranks, launches per step, clocks)."""
+    import torch
+
+    from clove_b200 import launch_count
+    for _ in range(max(warmup, 3)):
+        case.step()
+    torch.cuda.synchronize()
+    if case.pool.decode_status(case.lay.batch, case.q.shape[1], case.max_ctx) != 0:
+        raise RuntimeError(f"device check flags raised on the {case.spec.name} workload")
+    n0 = launch_count()
+    case.step()
+    torch.cuda.synchronize()
+    per_step = launch_count() - n0
+    run = case.step
+    if graph:
+        # the timed region then holds only device work (plan, decode,
+        # combine, and the all-gather under head sharding), not Python
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            case.step()
+        g.replay()
+        torch.cuda.synchronize()
+        run = g.replay
+    stream = torch.cuda.current_stream(case.dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(case.ws)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for _ in range(steps):
+            run()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    _barrier(case.ws)
+    ms = ev0.elapsed_time(ev1) / steps
+    return ms, _max_over_ranks(ms, case.ws, case.dev), per_step, clocks.summary()
+
+
+def phase_breakdown(case: DecodeCase, reps: int = 20) -> dict:
+    """Per-launch device times of one step, from CUDA events around each
+    launch (eager, serialised: the programmatic overlap of the plan ->
+    decode -> combine chain is lost, as in a profiler's launch list), the
+    median over `reps` steps, max over ranks."""
+    import ctypes as C
+
+    import torch
+
+    from clove_b200 import _lib
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(case.dev)
+    rows = []
+    L.clove_cuda_debug_phase_timing(1)
+    try:
+        for _ in range(reps + 2):
+            case.decode()
+            pl, de, co = C.c_float(), C.c_float(), C.c_float()
+            _lib.check(L.clove_cuda_debug_phase_ms(C.byref(pl), C.byref(de), C.byref(co)))
+            ag = 0.0
+            if case.head_split:
+                _barrier(case.ws)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                case.gather()
+                e1.record(stream)
+                e1.synchronize()
+                ag = e0.elapsed_time(e1)
+            rows.append((pl.value, de.value, co.value, ag))
+    finally:
+        L.clove_cuda_debug_phase_timing(0)
+    rows = rows[2:]
+    med = [statistics.median(r[i] for r in rows) for i in range(4)]
+    med = [_max_over_ranks(x, case.ws, case.dev) for x in med]
+    out = {"plan_ms": med[0], "decode_ms": med[1], "combine_ms": med[2]}
+    if case.head_split:
+        out["all_gather_ms"] = med[3]
+    out["note"] = "CUDA events around each launch, eager and serialised (median of %d steps, max over ranks)" % reps
+    return out
+
+
+def config_record(case: DecodeCase, ms_max: float, peak: float, launches: int | None = None) -> dict:
+    ws = case.ws
+    # KV bytes per GPU per step at the job's step time (slowest rank)
+    achieved = case.kv_total / ws / (ms_max * 1e-3) / 1e9
+    rec = {"value": case.global_batch / (ms_max * 1e-3), "unit": "tokens/s", "ms_per_step": ms_max,
+           "hbm_gbs": achieved, "global_batch": case.global_batch, "batch_per_gpu": case.lay.batch,
+           "kv_bytes_per_step": case.kv_total, "dtype": _dtype_name(case.spec.dtype),
+           "partition": _partition(case.mode, case.spec.name, ws),
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                        "frac": achieved / peak}}
+    if launches is not None:
+        rec["gpu_launches_per_step"] = launches
+    return rec
+
+
+def _policy(name: str) -> str:
+    from clove_b200.workload import SHARD_POLICY
+    return {"contiguous": "distribute_batch contiguous split", "tokens": "token-balanced"}[
+        SHARD_POLICY.get(name, "contiguous")]
+
+
+def run_ours(args) -> None:
+    import gc
+
+    import torch
 
     ws, rank, local = _dist()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    spec = CONFIGS[args.config]
-    if args.batch is not None:
-        spec = replace(spec, num_blocks=0)  # pool sized to the blocks used (profiling)
-    # c4 on N > 1 GPUs: KV heads split across ranks + one all-gather of the
-    # outputs (strong scaling: the same 8 sequences).  Every other run: one full
-    # workload per rank, sequences independent (weak scaling).
-    head_split = spec.name == "c4" and ws > 1
-    if head_split:
-        lay = make_layout(spec, seed=spec.seed, batch=args.batch)  # same tables on every rank
-        lspec = replace(spec, num_kv_heads=spec.num_kv_heads // ws, num_q_heads=spec.num_q_heads // ws,
-                        seed=spec.seed + rank)
-        llay = replace(lay, spec=lspec, seed=lspec.seed)
-        pool = KVPool(lay.num_blocks, spec.block_size, lspec.num_kv_heads, spec.head_dim, spec.dtype, dev)
-        _, kn, vn, _ = fill_values(llay, dev, pool.storage)
-        gq = torch.Generator(device=dev)
-        gq.manual_seed(spec.seed)
-        q_all = torch.randn((lay.batch, spec.num_q_heads, spec.head_dim), generator=gq, device=dev).to(spec.dtype)
-        hl = spec.num_q_heads // ws
-        q = q_all[:, rank * hl:(rank + 1) * hl].contiguous()  # this rank's query heads
-        gbuf = torch.empty((ws * lay.batch, hl, spec.head_dim), dtype=torch.float32, device=dev)
-    else:
-        lay = make_layout(spec, seed=spec.seed + rank, batch=args.batch)
-        pool = KVPool(lay.num_blocks, spec.block_size, spec.num_kv_heads, spec.head_dim, spec.dtype, dev)
-        q, kn, vn, _ = fill_values(lay, dev, pool.storage)
-    bt = torch.from_numpy(lay.block_tables).to(dev)
-    cl = torch.from_numpy(lay.context_lens).to(dev)
-    out = torch.empty((lay.batch, q.shape[1], spec.head_dim), dtype=torch.float32, device=dev)
-    max_ctx = lay.max_ctx
-    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = _peaks()
 
-    def step():
-        # launches on the current stream (the capture stream while a graph is recorded)
-        if head_split:
-            return head_sharded_append_decode(pool, q, kn, vn, bt, cl, ws, max_ctx, out_local=out, gather_buf=gbuf)
-        return pool.append_decode(q, kn, vn, bt, cl, max_ctx=max_ctx, out=out)
-
-    def barrier():
-        if ws > 1:
-            dist.barrier()
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    if pool.decode_status(lay.batch, q.shape[1], max_ctx) != 0:
-        raise RuntimeError("device check flags raised on the bench workload")
-    n0 = launch_count()
-    step()
-    torch.cuda.synchronize()
-    launches_per_step = launch_count() - n0
-    # One step captured in a CUDA graph and replayed: the timed region then
-    # holds only device work (plan, decode, combine, and the all-gather under
-    # head sharding), not Python launch overhead.
-    run = step
-    if not args.no_graph:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        graph.replay()
-        torch.cuda.synchronize()
-        run = graph.replay
-
-    # ---- device-timed region: inputs resident in HBM ----
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            run()
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    launches = launches_per_step * args.steps
-    ms = ev0.elapsed_time(ev1) / args.steps
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    # ---- headline: the configured workload (c2 by default) ----
+    case = DecodeCase(args.config, ws, rank, dev, batch=args.batch, weak=args.weak)
+    spec, lay = case.spec, case.lay
+    ms, ms_max, per_step, clocks = time_case(case, args.steps, args.warmup, graph=not args.no_graph, local=local)
+    launches = per_step * args.steps
+    breakdown = phase_breakdown(case)
 
     # ---- end to end: host (pinned) inputs -> device -> result back to host ----
-    hq = q.cpu().pin_memory()
-    hk, hv = kn.cpu().pin_memory(), vn.cpu().pin_memory()
-    hbt, hcl = bt.cpu().pin_memory(), cl.cpu().pin_memory()
-    hout = torch.empty((lay.batch, ws, out.shape[1], spec.head_dim) if head_split else out.shape,
+    hq = case.q.cpu().pin_memory()
+    hk, hv = case.kn.cpu().pin_memory(), case.vn.cpu().pin_memory()
+    hbt, hcl = case.bt.cpu().pin_memory(), case.cl.cpu().pin_memory()
+    out = case.out
+    hout = torch.empty((lay.batch, ws, out.shape[1], spec.head_dim) if case.head_split else out.shape,
                        dtype=torch.float32).pin_memory()
     dq, dk, dv, dbt, dcl = (torch.empty_like(x, device=dev) for x in (hq, hk, hv, hbt, hcl))
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hbt, hcl))
     d2h = hout.numel() * 4
+    stream = torch.cuda.current_stream(dev)
 
-    if head_split:
+    if case.head_split:
         def e2e_step():
             for d, h in ((dq, hq), (dk, hk), (dv, hv), (dbt, hbt), (dcl, hcl)):
                 d.copy_(h, non_blocking=True)
-            res = head_sharded_append_decode(pool, dq, dk, dv, dbt, dcl, ws, max_ctx, out_local=out,
-                                             gather_buf=gbuf)
+            res = case._hs(case.pool, dq, dk, dv, dbt, dcl, ws, case.max_ctx, out_local=out, gather_buf=case.gbuf)
             hout.copy_(res, non_blocking=True)
     else:
         # Through the reference-facing FFI (include/clove_ffi.h): tensors made
@@ -299,8 +512,8 @@ def run_ours(args) -> None:
                 raise RuntimeError(_lib.last_error())
             return h
 
-        kv_shape = (C.c_int64 * 5)(*pool.storage.shape)
-        kv_h = L.clove_tensor_from_device(pool.storage.data_ptr(), kv_shape, 5, code, local)
+        kv_shape = (C.c_int64 * 5)(*case.pool.storage.shape)
+        kv_h = L.clove_tensor_from_device(case.pool.storage.data_ptr(), kv_shape, 5, code, local)
         hq2, hk2, hv2 = hq.view(lay.batch, -1), hk.view(lay.batch, -1), hv.view(lay.batch, -1)
 
         def e2e_step():
@@ -314,52 +527,70 @@ def run_ours(args) -> None:
 
     for _ in range(3):
         e2e_step()
-    barrier()
+    _barrier(ws)
     torch.cuda.synchronize()
-    e2e_stream = stream if head_split else torch.cuda.default_stream(dev)  # the FFI runs on the legacy stream
+    e2e_stream = stream if case.head_split else torch.cuda.default_stream(dev)  # the FFI runs on the legacy stream
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(e2e_stream)
     for _ in range(args.steps):
         e2e_step()
     ev1.record(e2e_stream)
     torch.cuda.synchronize()
-    te = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item())
+    e2e_ms = _max_over_ranks(ev0.elapsed_time(ev1) / args.steps, ws, dev)
+    if not case.head_split:
+        kv_h and _lib.lib().clove_tensor_free(kv_h)
+    head = config_record(case, ms_max, peak, per_step)
+    del hq, hk, hv, hbt, hcl, hout, dq, dk, dv, dbt, dcl
+    case.close()
+    del case
+    gc.collect()
+    torch.cuda.empty_cache()
+
+    # ---- the other configurations at the same N, measured in the same run ----
+    per_config = {}
+    if args.per_config and args.batch is None:
+        for name in [c for c in ("c2", "c3", "c4", "c5") if c != args.config]:
+            c = DecodeCase(name, ws, rank, dev, weak=args.weak)
+            _, cmax, cper, _ = time_case(c, args.steps, args.warmup, local=local)
+            rec = config_record(c, cmax, peak, cper)
+            rec["phases"] = phase_breakdown(c)
+            per_config[name] = rec
+            c.close()
+            del c
+            gc.collect()
+            torch.cuda.empty_cache()
 
     if rank != 0:
         return
-    tokens = lay.batch * (1 if head_split else ws)
-    kv_bytes = lay.kv_bytes() // (ws if head_split else 1)  # per rank per step
-    achieved = kv_bytes / (ms * 1e-3) / 1e9
-    peak, peak_kind = _peaks()
     cb = None
-    if args.cpu_seconds > 0:
-        _, case = host_sample_case(spec, args.cpu_seqs)
-        cb = cpu_arm(lay, case, args.cpu_seconds)
+    if args.cpu_seconds > 0 and ws == 1:
+        lay_s, sample = host_sample_case(spec, args.cpu_seqs)
+        cb = cpu_arm(lay_s, sample, args.cpu_seconds)
+    achieved = head["hbm_gbs"]
+    traffic = args.traffic if args.traffic is not None else (
+        None if (args.batch is not None or ws > 1) else TRAFFIC_MEASURED.get(spec.name))
     line = {
-        "metric": METRIC, "value": tokens / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+        "metric": METRIC, "value": head["value"], "unit": "tokens/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-        "scaling": "strong" if head_split else "weak", "vs_baseline": None, "dtype": _dtype_name(spec.dtype),
-        "data": "synthetic",
-        "config": {"workload": spec.name, "description": spec.description, "batch_per_gpu": lay.batch,
-                   "global_batch": tokens, "num_q_heads": spec.num_q_heads, "num_kv_heads": spec.num_kv_heads,
-                   "head_dim": spec.head_dim, "block_size": spec.block_size, "num_blocks": lay.num_blocks,
-                   "kv_bytes_per_gpu_step": kv_bytes, "l2": "inputs larger than L2 (no flush)",
-                   "parallelism": (f"kv-heads/{ws} + all-gather" if head_split
-                                   else f"dp{ws} (independent sequences per GPU)")},
+        "scaling": "weak" if head["partition"].endswith("replicas") else "strong",
+        "vs_baseline": None, "dtype": _dtype_name(spec.dtype), "data": "synthetic",
+        "config": headline_config(args.config, ws, args.weak, args.batch),
         "hbm_gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak,
-                     "traffic": (args.traffic if args.traffic is not None
-                                 else None if (args.batch is not None or head_split)
-                                 else TRAFFIC_MEASURED.get(spec.name)),
-                     "note": f"KV bytes per step / whole step time (plan + decode kernels), peak {peak_kind}"},
+                     "frac": achieved / peak, "traffic": traffic,
+                     "note": (f"achieved = KV bytes per GPU per step / step time of the slowest rank (plan + "
+                              f"decode + combine), peak {peak_kind}; traffic = DRAM bytes per decode launch "
+                              f"from an earlier full-size ncu capture of this workload (not this run)"
+                              if traffic is not None else
+                              f"achieved = KV bytes per GPU per step / step time of the slowest rank, "
+                              f"peak {peak_kind}; no ncu capture of this exact case")},
+        "phases": breakdown,
         "gpu_launches": launches,
-        "clocks": clocks.summary(),
-        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+        "clocks": clocks,
+        "e2e": {"value": head["global_batch"] / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "cpu_baseline": cb,
+        "per_config": per_config,
     }
     print(json.dumps(line), flush=True)
 
@@ -492,6 +723,10 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=None, help="override the config batch (profiling only)")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a captured CUDA graph")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--weak", action="store_true",
+                    help="N>1: every rank runs a full replica of the workload instead of a shard of it")
+    ap.add_argument("--no-per-config", dest="per_config", action="store_false",
+                    help="skip the c2-c5 records measured after the headline")
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per decode launch from an ncu capture (reported as roofline.traffic)")
     args = ap.parse_args()

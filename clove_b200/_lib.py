@@ -55,6 +55,7 @@ SIGNATURES = {
     "clove_cuda_paged_append_decode": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _i, _vp, _i, _f, _i, _vp, _vp,
                                             _sz, _vp]),
     "clove_cuda_paged_append_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _i, _vp, _i, _f, _i, _vp, _vp]),
+    "clove_cuda_noalloc_status": (_i, [_i, _vp, _ip]),
     "clove_cuda_prefill_workspace_size": (_sz, [_vp, _i, _i, _i, _i]),
     "clove_cuda_paged_prefill": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _f, _f, _i, _vp, _vp, _sz,
                                       _vp]),
@@ -66,6 +67,8 @@ SIGNATURES = {
     "clove_cuda_set_decode_variant": (_i, [_i]),
     "clove_cuda_launch_count": (C.c_uint64, []),
     "clove_cuda_debug_set": (_i, [C.c_uint32, _i]),
+    "clove_cuda_debug_phase_timing": (_i, [_i]),
+    "clove_cuda_debug_phase_ms": (_i, [C.POINTER(_f), C.POINTER(_f), C.POINTER(_f)]),
 }
 
 

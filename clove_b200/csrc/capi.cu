@@ -501,6 +501,15 @@ int clove_cuda_set_decode_variant(int variant) {
 
 uint64_t clove_cuda_launch_count(void) { return g_launches.load(); }
 
+int clove_cuda_debug_phase_timing(int enable) {
+  set_phase_timing(enable);
+  return CLOVE_OK;
+}
+
+int clove_cuda_debug_phase_ms(float* plan_ms, float* decode_ms, float* combine_ms) {
+  return read_phase_ms(plan_ms, decode_ms, combine_ms);
+}
+
 int clove_cuda_debug_set(uint32_t wait_limit, int inject_stall) {
   g_wait_limit.store(wait_limit ? wait_limit : (1u << 24));
   g_inject_stall.store(inject_stall ? 1 : 0);

@@ -31,6 +31,7 @@
 // (src/nn/attention.rs:52-69), scale 1/sqrt(head_dim) supplied by the caller
 // (src/lazy.rs:5267), block-table gather of src/lazy.rs:5259-5270.
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 #include <unordered_map>
@@ -558,6 +559,56 @@ static int dispatch_dim(const clove_pool& pool, DecodeArgs& a, cudaStream_t stre
   }
 }
 
+// Phase timing (measurement hook): CUDA events around the plan, decode and
+// combine launches of the most recent call.  The events sit between the
+// launches, so while timing is on the programmatic overlap of consecutive
+// launches is lost; the phases are then serialised, as in a profiler's
+// launch list.
+static std::atomic<int> g_phase_timing{0};
+static std::mutex g_phase_mu;
+static cudaEvent_t g_phase_ev[4] = {nullptr, nullptr, nullptr, nullptr};
+static int g_phase_dev = -1;
+static bool g_phase_recorded = false;
+
+static void phase_mark(int i, cudaStream_t stream) {
+  if (!g_phase_timing.load(std::memory_order_relaxed)) return;
+  std::lock_guard<std::mutex> lk(g_phase_mu);
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (dev != g_phase_dev) {
+    for (auto& e : g_phase_ev)
+      if (e) {
+        cudaEventDestroy(e);
+        e = nullptr;
+      }
+    g_phase_dev = dev;
+  }
+  if (!g_phase_ev[i] && cudaEventCreate(&g_phase_ev[i]) != cudaSuccess) return;
+  cudaEventRecord(g_phase_ev[i], stream);
+  if (i == 3) g_phase_recorded = true;
+}
+
+void set_phase_timing(int on) { g_phase_timing.store(on ? 1 : 0); }
+
+int read_phase_ms(float* plan_ms, float* decode_ms, float* combine_ms) {
+  std::lock_guard<std::mutex> lk(g_phase_mu);
+  if (!g_phase_recorded) {
+    set_last_error("debug_phase_ms: no decode was timed (enable with clove_cuda_debug_phase_timing)");
+    return CLOVE_ERR_INVALID_ARG;
+  }
+  cudaError_t e = cudaEventSynchronize(g_phase_ev[3]);
+  float t[3] = {0.f, 0.f, 0.f};
+  for (int i = 0; i < 3 && e == cudaSuccess; ++i) e = cudaEventElapsedTime(&t[i], g_phase_ev[i], g_phase_ev[i + 1]);
+  if (e != cudaSuccess) {
+    set_last_error("debug_phase_ms: %s", cudaGetErrorString(e));
+    return CLOVE_ERR_CUDA;
+  }
+  if (plan_ms) *plan_ms = t[0];
+  if (decode_ms) *decode_ms = t[1];
+  if (combine_ms) *combine_ms = t[2];
+  return CLOVE_OK;
+}
+
 int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t stream) {
   const DecodeLayout L = decode_layout(pool, call.batch, call.num_q_heads, call.max_ctx);
   if (call.workspace_bytes < L.total) {
@@ -589,6 +640,7 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   p.multi = reinterpret_cast<int32_t*>(ws + L.off_multi);
   p.max_ctx = call.max_ctx;
   p.append = append;
+  phase_mark(0, stream);
   plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -596,6 +648,7 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
     return CLOVE_ERR_CUDA;
   }
   count_launches(1);
+  phase_mark(1, stream);
 
   DecodeArgs a;
   a.q = call.q;
@@ -639,7 +692,12 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
       set_last_error("paged_decode: dtype %d", pool.dtype);
       return CLOVE_ERR_UNSUPPORTED;
   }
-  if (rc != CLOVE_OK || L.max_chunks <= 1) return rc;
+  if (rc != CLOVE_OK) return rc;
+  phase_mark(2, stream);
+  if (L.max_chunks <= 1) {
+    phase_mark(3, stream);
+    return rc;
+  }
   // Split-K combine for the sequences the plan split into several chunks.
   {
     cudaLaunchConfig_t cfg = {};
@@ -659,6 +717,7 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
     }
     count_launches(1);
   }
+  phase_mark(3, stream);
   return CLOVE_OK;
 }
 

@@ -42,8 +42,9 @@ struct DeviceCache {
   std::mutex mu;
   std::unordered_map<size_t, std::vector<void*>> free_lists;
   size_t held = 0;
-  void* workspace = nullptr;
+  void* workspace = nullptr;  // cudaMallocAsync'd on the legacy stream (stream-ordered free on growth)
   size_t workspace_bytes = 0;
+  int32_t* flags_host = nullptr;  // pinned word: the check flags of the last decode, read after it
 };
 
 constexpr int kMaxDev = 64;
@@ -252,43 +253,52 @@ CTensor clove_paged_attention(CTensor q, CTensor k, CTensor v, CTensor kv, CTens
                                   &kv->pool);
     if (rc) return nullptr;
   }
-  // max_ctx (tokens attended) from the host copy of context_lens when the
-  // tensor was made from host data, else one device-to-host read.
-  std::vector<int32_t> tmp;
-  const std::vector<int32_t>* lens = &cl->host_i32;
-  if ((int)cl->host_i32.size() != batch) {
-    tmp.resize(batch);
-    if (batch && (cudaMemcpy(tmp.data(), cl->ptr, 4 * (size_t)batch, cudaMemcpyDeviceToHost) != cudaSuccess)) {
-      set_last_error("paged_attention: reading context_lens failed");
-      return nullptr;
-    }
-    lens = &tmp;
+  // max_ctx (tokens attended): from the host copy of context_lens when the
+  // tensor was made from host data, else the block table's capacity (no
+  // device-to-host read on the call path; the kernels flag lengths beyond it).
+  long long max_ctx = (long long)bt->shape[1] * bs;
+  if ((int)cl->host_i32.size() == batch) {
+    long long m = 1;
+    for (int32_t c : cl->host_i32) m = std::max<long long>(m, (long long)c + 1);
+    max_ctx = std::min(max_ctx, m);
   }
-  int max_ctx = 1;
-  for (int32_t c : *lens) max_ctx = std::max(max_ctx, c + 1);
-  max_ctx = std::min<long long>(max_ctx, (long long)bt->shape[1] * bs);
+  if (max_ctx < 1) max_ctx = 1;
+  if (max_ctx > INT32_MAX) {
+    set_last_error("paged_attention: block table of %lld tokens per sequence is too large", max_ctx);
+    return nullptr;
+  }
   const int64_t oshape[2] = {batch, (int64_t)hq * d};
   CTensor out = clove_tensor_create_nd(nullptr, oshape, 2, CLOVE_DTYPE_F32, dev);
   if (!out) return nullptr;
-  const size_t need = clove_cuda_decode_workspace_size(kv->pool, batch, hq, max_ctx);
+  const size_t need = clove_cuda_decode_workspace_size(kv->pool, batch, hq, (int)max_ctx);
   DeviceCache& c = g_cache[dev];
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  int32_t* flags_host = nullptr;
   {
     std::lock_guard<std::mutex> lk(c.mu);
+    if (!c.flags_host && cudaMallocHost(reinterpret_cast<void**>(&c.flags_host), sizeof(int32_t)) != cudaSuccess) {
+      c.flags_host = nullptr;
+      cudaGetLastError();
+    }
     if (c.workspace_bytes < need) {
-      if (c.workspace) {
-        cudaDeviceSynchronize();  // the old workspace may be in use by queued work
-        cudaFree(c.workspace);
-      }
+      // Stream-ordered: queued decodes on the legacy stream finish with the
+      // old buffer before it is released; the host does not wait.
+      if (c.workspace) cudaFreeAsync(c.workspace, 0);
       c.workspace = nullptr;
       c.workspace_bytes = 0;
-      if (cudaMalloc(&c.workspace, round_cap(need)) == cudaSuccess) c.workspace_bytes = round_cap(need);
+      if (cudaMallocAsync(&c.workspace, round_cap(need), 0) == cudaSuccess) {
+        c.workspace_bytes = round_cap(need);
+      } else {
+        c.workspace = nullptr;
+        cudaGetLastError();
+      }
     }
     ws = c.workspace;
     ws_bytes = c.workspace_bytes;
+    flags_host = c.flags_host;
   }
-  if (!ws) {
+  if (!ws || !flags_host) {
     clove_tensor_free(out);
     set_last_error("paged_attention: workspace allocation of %zu bytes failed", need);
     return nullptr;
@@ -296,9 +306,30 @@ CTensor clove_paged_attention(CTensor q, CTensor k, CTensor v, CTensor kv, CTens
   const float scale = 1.0f / std::sqrt((float)d);
   int rc = clove_cuda_paged_append_decode(kv->pool, q->ptr, k->ptr, v->ptr, hq, static_cast<const int32_t*>(bt->ptr),
                                           (int)bt->shape[1], static_cast<const int32_t*>(cl->ptr), batch, scale,
-                                          max_ctx, static_cast<float*>(out->ptr), ws, ws_bytes, nullptr);
+                                          (int)max_ctx, static_cast<float*>(out->ptr), ws, ws_bytes, nullptr);
   if (rc) {
     clove_tensor_free(out);
+    return nullptr;
+  }
+  // Device-side checks: the decode's check-flag word (bad block ids, context
+  // lengths beyond the table, a pipeline wait that ran out).  The reference
+  // op is synchronous and aborts on bad input; here the call waits for the
+  // decode and returns NULL with the flags in the error text instead of a
+  // silently clamped result.
+  if (cudaMemcpyAsync(flags_host, ws, sizeof(int32_t), cudaMemcpyDeviceToHost, 0) != cudaSuccess ||
+      cudaStreamSynchronize(0) != cudaSuccess) {
+    clove_tensor_free(out);
+    set_last_error("paged_attention: %s", cudaGetErrorString(cudaGetLastError()));
+    return nullptr;
+  }
+  if (*flags_host) {
+    const int f = *flags_host;
+    clove_tensor_free(out);
+    set_last_error("paged_attention: device check flags 0x%x:%s%s%s%s", f,
+                   (f & CLOVE_FLAG_BLOCK_OOB) ? " block id outside the pool;" : "",
+                   (f & CLOVE_FLAG_CTX_RANGE) ? " context length outside [0, block table capacity);" : "",
+                   (f & CLOVE_FLAG_SLOT_OOB) ? " slot outside the pool;" : "",
+                   (f & CLOVE_FLAG_TIMEOUT) ? " a pipeline wait ran out;" : "");
     return nullptr;
   }
   return out;

@@ -105,5 +105,7 @@ void count_launches(int n);
 int decode_variant();  // 0 auto, 1 simt, 2 mma
 uint32_t debug_wait_limit();
 int debug_inject_stall();
+void set_phase_timing(int on);  // decode_kernels.cu
+int read_phase_ms(float* plan_ms, float* decode_ms, float* combine_ms);
 
 }  // namespace clove

@@ -6,8 +6,10 @@
 // call on the serving path, or a plugin host that forbids cudaMalloc after
 // start-up.  clove_cuda_paged_append_decode_noalloc serves them: it runs the
 // same append + decode as clove_cuda_paged_append_decode, with its scratch in
-// a fixed array that this library places in every GPU's memory when the GPU
-// first loads it and keeps until the process exits.
+// a fixed array of this library's device code.  The array is placed in a
+// GPU's memory when the library's device code is first loaded on that GPU
+// (with CUDA's lazy module loading: at the first use of any of the library's
+// kernels or symbols there) and stays until the process exits.
 //
 // Limits and rules:
 //   - The scratch is kNoAllocScratchBytes (32 MiB) per GPU; calls whose
@@ -20,7 +22,10 @@
 //     serialise them.
 //   - The first call on a device looks up the array's device address (with
 //     that device current) and caches it; make that first call before any
-//     stream capture.
+//     stream capture.  A failed lookup is not cached: the next call retries.
+//   - Device check flags (bad block ids, context lengths, a bounded wait that
+//     ran out) land in the array's first word, like the workspace call's;
+//     clove_cuda_noalloc_status reads and clears them.
 #include <mutex>
 
 #include "host.h"
@@ -35,18 +40,48 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 static void* g_scratch_ptr[kMaxDevices] = {};
-static std::once_flag g_scratch_once[kMaxDevices];
-static cudaError_t g_scratch_err[kMaxDevices] = {};
+static std::mutex g_scratch_mu;
 
-// Device address of the scratch on `device` (which must be current).
+// Device address of the scratch on `device` (which must be current).  Only a
+// successful lookup is cached; after a failure (e.g. a first call made during
+// stream capture) the error is cleared and the next call tries again.
 static void* scratch_on(int device, cudaError_t* err) {
-  std::call_once(g_scratch_once[device], [device] {
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  *err = cudaSuccess;
+  if (!g_scratch_ptr[device]) {
     void* p = nullptr;
-    g_scratch_err[device] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    g_scratch_ptr[device] = g_scratch_err[device] == cudaSuccess ? p : nullptr;
-  });
-  *err = g_scratch_err[device];
+    *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (*err == cudaSuccess) {
+      g_scratch_ptr[device] = p;
+    } else {
+      cudaGetLastError();
+    }
+  }
   return g_scratch_ptr[device];
+}
+
+// The scratch address on `device`, made current for the lookup and then
+// restored.  Returns a CLOVE_* status.
+static int scratch_for(int device, const char* who, void** ws) {
+  if (device < 0 || device >= kMaxDevices) {
+    set_last_error("%s: device %d beyond %d", who, device, kMaxDevices);
+    return CLOVE_ERR_NO_DEVICE;
+  }
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  if (prev != device && cudaSetDevice(device) != cudaSuccess) {
+    cudaGetLastError();
+    set_last_error("%s: cudaSetDevice(%d) failed", who, device);
+    return CLOVE_ERR_CUDA;
+  }
+  cudaError_t e = cudaSuccess;
+  *ws = scratch_on(device, &e);
+  if (prev >= 0 && prev != device) cudaSetDevice(prev);
+  if (!*ws) {
+    set_last_error("%s: cudaGetSymbolAddress: %s", who, cudaGetErrorString(e));
+    return CLOVE_ERR_CUDA;
+  }
+  return CLOVE_OK;
 }
 
 }  // namespace clove
@@ -63,10 +98,6 @@ int clove_cuda_paged_append_decode_noalloc(clove_pool_t pool, const void* q, con
     set_last_error("paged_append_decode_noalloc: null pool");
     return CLOVE_ERR_INVALID_ARG;
   }
-  if (pool->device < 0 || pool->device >= kMaxDevices) {
-    set_last_error("paged_append_decode_noalloc: device %d beyond %d", pool->device, kMaxDevices);
-    return CLOVE_ERR_NO_DEVICE;
-  }
   if (batch <= 0 || num_q_heads <= 0 || max_ctx < 1) {
     // Same argument checks (and messages) as the workspace entry point.
     return clove_cuda_paged_append_decode(pool, q, k_new, v_new, num_q_heads, block_tables, bt_stride,
@@ -80,21 +111,18 @@ int clove_cuda_paged_append_decode_noalloc(clove_pool_t pool, const void* q, con
         need, kNoAllocScratchBytes);
     return CLOVE_ERR_WORKSPACE;
   }
-  int prev = -1;
-  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-  if (prev != pool->device && cudaSetDevice(pool->device) != cudaSuccess) {
-    set_last_error("paged_append_decode_noalloc: cudaSetDevice(%d) failed", pool->device);
-    return CLOVE_ERR_CUDA;
-  }
-  cudaError_t e = cudaSuccess;
-  void* ws = scratch_on(pool->device, &e);
-  if (prev >= 0 && prev != pool->device) cudaSetDevice(prev);
-  if (!ws) {
-    set_last_error("paged_append_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    return CLOVE_ERR_CUDA;
-  }
+  void* ws = nullptr;
+  const int rc = scratch_for(pool->device, "paged_append_decode_noalloc", &ws);
+  if (rc != CLOVE_OK) return rc;
   return clove_cuda_paged_append_decode(pool, q, k_new, v_new, num_q_heads, block_tables, bt_stride, context_lens,
                                         batch, scale, max_ctx, out, ws, kNoAllocScratchBytes, stream);
+}
+
+int clove_cuda_noalloc_status(int device, void* stream, int* flags) {
+  void* ws = nullptr;
+  const int rc = scratch_for(device, "noalloc_status", &ws);
+  if (rc != CLOVE_OK) return rc;
+  return clove_cuda_decode_status(ws, stream, flags);
 }
 
 }  // extern "C"

@@ -136,13 +136,16 @@ def compile(graph: LazyGraph, outputs: list[LazyTensor]) -> list[Step]:
             for d in node.deps:
                 users[d] = users.get(d, 0) + 1
     # MatMul + bias Add -> one Linear step (the reference Linear, src/nn.rs:114-117),
-    # run as one GEMM with the bias in its epilogue
+    # run as one GEMM with the bias in its epilogue.  A MatMul that is itself
+    # a requested output keeps its own step (its value must exist).
+    requested = {t.id for t in outputs}
     fused_mm: set[int] = set()
     linear_of: dict[int, list[int]] = {}
     for node in graph.nodes:
         if node.id in need and node.op is Opcode.ADD:
             mm = graph.nodes[node.deps[0]]
-            if mm.op is Opcode.MATMUL and users.get(mm.id) == 1 and len(graph.nodes[node.deps[1]].shape) == 1:
+            if (mm.op is Opcode.MATMUL and users.get(mm.id) == 1 and mm.id not in requested
+                    and len(graph.nodes[node.deps[1]].shape) == 1):
                 fused_mm.add(mm.id)
                 linear_of[node.id] = [mm.deps[0], mm.deps[1], node.deps[1]]
     steps: list[Step] = []

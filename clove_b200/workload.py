@@ -14,7 +14,7 @@ over ctx + 1 tokens):
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, replace
 
 import numpy as np
 import torch
@@ -93,13 +93,19 @@ def _context_lens(spec: Spec, rng: np.random.Generator, batch: int) -> np.ndarra
 
 
 def make_layout(spec: Spec, seed: int | None = None, batch: int | None = None,
-                ctx_scale: float = 1.0) -> Layout:
+                ctx_scale: float = 1.0, context_lens: np.ndarray | None = None) -> Layout:
     """Context lengths and block tables for `spec` (optionally a smaller
-    batch, or context lengths scaled down for CPU-sized parity cases)."""
+    batch, or context lengths scaled down for CPU-sized parity cases).  With
+    `context_lens`, those lengths are used as given and only the block
+    tables are drawn."""
     seed = spec.seed if seed is None else seed
     rng = np.random.default_rng(seed)
-    batch = spec.batch if batch is None else batch
-    ctx = _context_lens(spec, rng, batch)
+    if context_lens is not None:
+        ctx = np.asarray(context_lens, np.int32)
+        batch = int(ctx.shape[0])
+    else:
+        batch = spec.batch if batch is None else batch
+        ctx = _context_lens(spec, rng, batch)
     if ctx_scale != 1.0:
         ctx = np.maximum(1, np.rint(ctx * ctx_scale)).astype(np.int32)
     bs = spec.block_size
@@ -133,6 +139,39 @@ def make_layout(spec: Spec, seed: int | None = None, batch: int | None = None,
         bt[b, :n] = ids[off: off + n]
         off += n
     return Layout(spec, ctx, bt, nb, seed)
+
+
+# How each configuration's batch shards over GPUs (sequences are
+# independent; every rank owns its own block pool and tables).  c2 follows
+# distribute_batch's contiguous split; the ragged configurations balance
+# attended tokens.  c4 splits KV heads instead (see clove_b200.distributed).
+SHARD_POLICY = {"c1": "contiguous", "c2": "contiguous", "c3": "tokens", "c5": "tokens"}
+
+
+def shard_layout(spec: Spec, world: int, rank: int, policy: str | None = None,
+                 batch: int | None = None) -> tuple[Layout, np.ndarray]:
+    """Rank `rank`'s share of `spec`'s batch over `world` GPUs: the global
+    context lengths are drawn from the configuration's seed (identical on
+    every rank), the rank takes its sequences, and its own pool of
+    num_blocks / world blocks (derived when the spec derives it) gets block
+    tables drawn with the configuration's table rule and a rank-specific
+    seed.  Returns (layout, global sequence indices of this rank)."""
+    from .sharding import contiguous_shards, token_balanced_shards
+    glob = make_layout(spec, batch=batch)
+    if world <= 1:
+        return glob, np.arange(glob.batch)
+    policy = policy or SHARD_POLICY.get(spec.name, "contiguous")
+    if policy == "contiguous":
+        idx = contiguous_shards(glob.batch, world)[rank]
+    elif policy == "tokens":
+        idx = token_balanced_shards(glob.context_lens, world)[rank]
+    else:
+        raise ValueError(policy)
+    local = spec if not spec.num_blocks else replace(spec, num_blocks=max(1, spec.num_blocks // world))
+    lay = make_layout(local, seed=spec.seed + 7919 * (rank + 1), context_lens=glob.context_lens[idx])
+    lay.extra["global_batch"] = glob.batch
+    lay.extra["global_kv_bytes"] = glob.kv_bytes()
+    return lay, idx
 
 
 def fill_values(layout: Layout, device: torch.device | str, pool_storage: torch.Tensor | None = None,

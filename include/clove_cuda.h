@@ -238,12 +238,15 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x,
  * whose device memory comes only from an allocator it may not call on the
  * serving path).  No counterpart in the reference.  Same arguments and
  * results as clove_cuda_paged_append_decode, minus the workspace: scratch
- * comes from a fixed 32 MiB array the library keeps on every GPU that loads
- * it, until the process exits.  Returns CLOVE_ERR_WORKSPACE when the call
- * needs more than that (see clove_cuda_decode_workspace_size).  All calls on
- * a GPU share the array: calls that overlap on the GPU race, so serialise
- * them.  The first call on a device looks up the array's address; make it
- * before any stream capture.  The call allocates nothing. */
+ * comes from a fixed 32 MiB array in the library's device code, placed on a
+ * GPU when the library's device code is first loaded there and kept until
+ * the process exits.  Returns CLOVE_ERR_WORKSPACE when the call needs more
+ * than that (see clove_cuda_decode_workspace_size).  All calls on a GPU
+ * share the array: calls that overlap on the GPU race, so serialise them.
+ * The first call on a device looks up the array's address (a failed lookup
+ * is retried by the next call); make it before any stream capture.  Device
+ * check flags go to the array and are read with clove_cuda_noalloc_status.
+ * The call allocates nothing. */
 int clove_cuda_paged_append_decode_noalloc(clove_pool_t pool, const void* q,
                                            const void* k_new, const void* v_new,
                                            int num_q_heads,
@@ -252,6 +255,13 @@ int clove_cuda_paged_append_decode_noalloc(clove_pool_t pool, const void* q,
                                            const int32_t* context_lens,
                                            int batch, float scale, int max_ctx,
                                            float* out, void* stream);
+
+/* Check flags (CLOVE_FLAG_*) of the most recent
+ * clove_cuda_paged_append_decode_noalloc call on `device`: synchronises
+ * `stream`, reads and clears the flag word of the built-in scratch, like
+ * clove_cuda_decode_status does for a caller workspace.  No counterpart in
+ * the reference. */
+int clove_cuda_noalloc_status(int device, void* stream, int* flags);
 
 /* Synchronise `stream` and read the device check flags (CLOVE_FLAG_*) that
  * the most recent decode call on `workspace` raised (each call clears them
@@ -275,6 +285,16 @@ uint64_t clove_cuda_launch_count(void);
  * CLOVE_FLAG_TIMEOUT through clove_cuda_decode_status, and its output is
  * undefined.  Process-wide; never set it in production. */
 int clove_cuda_debug_set(uint32_t wait_limit, int inject_stall);
+
+/* Measurement hook: with enable = 1, every decode call records CUDA events
+ * around its plan, decode and combine launches; clove_cuda_debug_phase_ms
+ * waits for the most recent timed call and returns the three durations in
+ * milliseconds (combine = 0 when the call needed no split-K merge).  The
+ * events sit between the launches, so timed calls lose the overlap of
+ * programmatically chained launches.  Process-wide; for the benchmark. */
+int clove_cuda_debug_phase_timing(int enable);
+int clove_cuda_debug_phase_ms(float* plan_ms, float* decode_ms,
+                              float* combine_ms);
 
 #ifdef __cplusplus
 }

@@ -15,7 +15,7 @@
  * buffers are kept for reuse, the idea of the reference's BufferPool,
  * src/device.rs:177-222), so a decode loop does not call cudaMalloc per step.
  * All copies and kernels run on the legacy default stream; clove_tensor_data
- * synchronises.
+ * and clove_paged_attention synchronise it.
  */
 #ifndef CLOVE_FFI_H
 #define CLOVE_FFI_H
@@ -58,8 +58,13 @@ int clove_tensor_shape(CTensor t, int64_t* shape);
  *   kv [2, num_blocks, block_size, Hkv, D] (K plane, V plane)
  *   bt int32 [B, max_blocks_per_seq]   cl int32 [B] (lengths before this token)
  * Appends k, v at slot bt[b][cl_b/bs]*bs + cl_b%bs, attends over cl_b + 1
- * tokens with scale 1/sqrt(D) and returns a new f32 [B, Hq*D] tensor; NULL on
- * error. */
+ * tokens with scale 1/sqrt(D) and returns a new f32 [B, Hq*D] tensor.  The
+ * call waits for the decode (the reference's op is synchronous) and checks
+ * the kernels' device flags: a block id outside the pool, a context length
+ * beyond the block table or a pipeline wait that ran out returns NULL with
+ * the flags in clove_cuda_get_last_error's text, never a clamped result.
+ * NULL on any error.  When cl was made from host data its maximum sizes the
+ * scratch; otherwise the table width does (no device-to-host read). */
 CTensor clove_paged_attention(CTensor q, CTensor k, CTensor v, CTensor kv, CTensor bt, CTensor cl);
 
 /* Bytes currently held by the handle cache of `device` (for tests). */

@@ -139,14 +139,39 @@ def mock_paged_attention(q: np.ndarray, kv_cache: np.ndarray, block_tables_1024:
     return out
 
 
+# Every tolerance check made in this process: (test id, rtol, worst
+# |x-r|/(|r|+rms), plain max |x-r|/|r|, fraction within plain rtol*|r|,
+# elements).  The test session prints a summary of it.
+PARITY_LOG: list[tuple] = []
+
+
+def plain_relative_error(x: np.ndarray, ref: np.ndarray, rtol: float) -> tuple[float, float]:
+    """(max |x - r| / |r| over the elements with r != 0, fraction of all
+    elements with |x - r| <= rtol * |r|)."""
+    x = np.asarray(x, np.float64)
+    r = np.asarray(ref, np.float64)
+    if not r.size:
+        return 0.0, 1.0
+    err = np.abs(x - r)
+    nz = r != 0
+    mx = float((err[nz] / np.abs(r[nz])).max()) if nz.any() else 0.0
+    return mx, float((err <= rtol * np.abs(r)).mean())
+
+
 def tolerance_ok(x: np.ndarray, ref: np.ndarray, rtol: float) -> tuple[bool, float]:
-    """|x - r| <= rtol * (|r| + rms(r)) elementwise; returns (ok, worst ratio)."""
+    """|x - r| <= rtol * (|r| + rms(r)) elementwise; returns (ok, worst ratio).
+    The plain relative error (max |x - r| / |r|) is logged beside it in
+    PARITY_LOG: near zeros of r it is large for any rounding, which is why
+    the bar adds rms(r) to |r|."""
     x = np.asarray(x, np.float64)
     r = np.asarray(ref, np.float64)
     rms = float(np.sqrt(np.mean(r * r))) if r.size else 0.0
     bound = rtol * (np.abs(r) + rms) + 1e-30
     ratio = np.abs(x - r) / bound
     worst = float(ratio.max()) * rtol if ratio.size else 0.0
+    plain, within = plain_relative_error(x, r, rtol)
+    PARITY_LOG.append((os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0], rtol, worst, plain, within,
+                       int(r.size)))
     return bool((ratio <= 1.0).all()), worst
 
 

@@ -39,3 +39,25 @@ def cuda_ok() -> bool:
 def _skip_gpu_without_cuda(request):
     if request.node.get_closest_marker("gpu") and not cuda_ok():
         pytest.skip("no CUDA device")
+
+
+def pytest_terminal_summary(terminalreporter):
+    """Parity summary: for every test that compared a CUDA result with the
+    oracle, the bar's worst |x-r|/(|r|+rms) next to the plain max relative
+    error |x-r|/|r| and the share of elements within rtol*|r|."""
+    try:
+        import oracle
+    except Exception:
+        return
+    log = oracle.PARITY_LOG
+    if not log:
+        return
+    per = {}
+    for tid, rtol, worst, plain, within, n in log:
+        w = per.setdefault(tid, [rtol, 0.0, 0.0, 1.0, 0])
+        w[1], w[2], w[3], w[4] = max(w[1], worst), max(w[2], plain), min(w[3], within), w[4] + n
+    tr = terminalreporter
+    tr.write_sep("-", f"parity vs oracle: {len(per)} tests")
+    tr.write_line(f"{'rtol':>7} {'worst(|r|+rms)':>14} {'plain max rel':>13} {'within rtol|r|':>14} {'elems':>9}  test")
+    for tid, (rtol, worst, plain, within, n) in sorted(per.items()):
+        tr.write_line(f"{rtol:7.0e} {worst:14.3e} {plain:13.3e} {within:14.6f} {n:9d}  {tid}")

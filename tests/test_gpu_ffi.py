@@ -65,3 +65,54 @@ def test_ffi_errors_return_null():
     assert not L.clove_paged_attention(q, k_bad, k_bad, kv_h, bt, cl_f)
     for h in (q, kv_h, bt, cl, k_bad, cl_f):
         L.clove_tensor_free(h)
+
+
+def test_ffi_bad_block_id_returns_null_with_flags():
+    """A block-table entry outside the pool is never followed: the call
+    returns NULL and the error text names the flag, instead of a clamped
+    answer."""
+    from clove_b200 import _lib
+    L = _lib.lib()
+    g = load_golden("f32_mha_small")
+    B, hq, d = g["q"].shape
+    kv = np.stack([g["k_cache"], g["v_cache"]])
+    bt_bad = g["block_tables"].copy()
+    bt_bad[1, 0] = kv.shape[1] + 5  # past the pool's last block
+    hs = [_t(L, g["q"].reshape(B, -1), 0), _t(L, g["k_new"].reshape(B, -1), 0), _t(L, g["v_new"].reshape(B, -1), 0),
+          _t(L, kv, 0), _t(L, bt_bad, _lib.DTYPE_I32), _t(L, g["context_lens"], _lib.DTYPE_I32)]
+    assert not L.clove_paged_attention(*hs)
+    msg = _lib.last_error()
+    assert "block id outside the pool" in msg, msg
+    # the next good call on the same handles works
+    good_bt = _t(L, g["block_tables"], _lib.DTYPE_I32)
+    out = L.clove_paged_attention(hs[0], hs[1], hs[2], hs[3], good_bt, hs[5])
+    assert out, _lib.last_error()
+    for h in hs + [good_bt, out]:
+        L.clove_tensor_free(h)
+
+
+def test_ffi_device_context_lens_without_host_copy():
+    """context_lens handed over as device memory: the call sizes its scratch
+    from the block table (no device-to-host read) and gives the same result
+    as the host-made tensor."""
+    import torch
+
+    import oracle
+    from clove_b200 import _lib
+    L = _lib.lib()
+    g = load_golden("f32_mha_small")
+    B, hq, d = g["q"].shape
+    kv = np.stack([g["k_cache"], g["v_cache"]])
+    cl_dev = torch.from_numpy(g["context_lens"].astype(np.int32)).cuda()
+    shp = (C.c_int64 * 1)(B)
+    cl_h = L.clove_tensor_from_device(cl_dev.data_ptr(), shp, 1, _lib.DTYPE_I32, 0)
+    hs = [_t(L, g["q"].reshape(B, -1), 0), _t(L, g["k_new"].reshape(B, -1), 0), _t(L, g["v_new"].reshape(B, -1), 0),
+          _t(L, kv, 0), _t(L, g["block_tables"], _lib.DTYPE_I32)]
+    out = L.clove_paged_attention(*hs, cl_h)
+    assert out, _lib.last_error()
+    host = np.empty((B, hq * d), np.float32)
+    L.clove_tensor_data(out, host.ctypes.data)
+    ok, worst = oracle.tolerance_ok(host.reshape(B, hq, d), g["expected"], 1e-5)
+    assert ok, worst
+    for h in hs + [cl_h, out]:
+        L.clove_tensor_free(h)

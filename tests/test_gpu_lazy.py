@@ -1,7 +1,8 @@
 """GPU: a traced-and-compiled PagedAttention::forward graph (projections +
 paged attention + output projection) dispatches PagedAttention to the CUDA
-path and gives the eager module's result bit for bit; a symbolic batch binds
-at execution."""
+path; its result is checked against the fp64 oracle of the whole module
+(Linear, append, decode, Linear) and equals the eager module's bit for bit;
+a symbolic batch binds at execution."""
 import numpy as np
 import pytest
 import torch
@@ -52,5 +53,29 @@ def test_compiled_forward_matches_eager(dtype, bs):
              "block_tables": btd, "context_lens": cld}
     lazy = execute(lb.graph, steps, feeds, max_ctx=max_ctx)[out.id]
     torch.cuda.synchronize()
+
+    # fp64 oracle of the module: the three projections (src/nn.rs:538-540,
+    # rounded to the cache dtype as the library GEMMs store them), the
+    # slot-mapping append, the decode (src/nn/attention.rs:52-69) and the
+    # output projection (src/nn.rs:545)
+    import oracle
+    from workload_check import tol_check
+
+    def lin(a, w, b):
+        return oracle.linear(a, w.double().cpu().numpy(), b.double().cpu().numpy())
+
+    def rnd(a):  # round to the module dtype, back to f32 (exact)
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dtype).float().numpy()
+
+    x64 = x.double().cpu().numpy()
+    qr = rnd(lin(x64, m.w_q.weight, m.w_q.bias)).reshape(B, hq, D)
+    kr = rnd(lin(x64, m.w_k.weight, m.w_k.bias)).reshape(B, hkv, D)
+    vr = rnd(lin(x64, m.w_v.weight, m.w_v.bias)).reshape(B, hkv, D)
+    kc, vc = kv0[0].float().cpu().numpy(), kv0[1].float().cpu().numpy()
+    assert oracle.reshape_and_cache(kc, vc, kr, vr, oracle.append_slots(bt, ctx, bs)) == 0
+    attn = oracle.decode_f64(oracle.F32, qr, kc, vc, bt, ctx + 1, 1.0 / np.sqrt(D))
+    ref = lin(attn.reshape(B, -1), m.w_o.weight, m.w_o.bias)
+    # bf16: the 16-bit bar; f32: three f32 library GEMMs around the decode
+    tol_check(lazy.double().cpu().numpy(), ref, 2e-2 if dtype == torch.bfloat16 else 1e-4)
     assert torch.equal(lazy, eager)
     assert torch.equal(kv_l.view(torch.uint8), kv_e.view(torch.uint8))  # same appended slots

@@ -84,3 +84,16 @@ def test_execute_binds_symbols_and_runs_linear_steps_on_any_device():
     s2 = lb2.add(a1, a2)
     with pytest.raises(ValueError, match="symbol B"):
         execute(lb2.graph, compile(lb2.graph, [s2]), {"a1": torch.zeros(2, 4), "a2": torch.zeros(3, 4)})
+
+
+def test_requested_matmul_is_not_fused_away():
+    # a MatMul that is also a requested output keeps its own step, so its
+    # value exists after execute(); the Add then runs as a plain step
+    lb = LazyBackend()
+    x, w, b = lb.input("x", (4, 64)), lb.input("w", (64, 32)), lb.input("b", (32,))
+    mm = lb.matmul(x, w)
+    y = lb.add(mm, b)
+    ops = [s.op for s in compile(lb.graph, [y, mm])]
+    assert Opcode.LINEAR not in ops
+    assert ops.count(Opcode.MATMUL) == 1 and ops.count(Opcode.ADD) == 1
+    assert [s.op for s in compile(lb.graph, [y])] == [Opcode.LINEAR]
