@@ -68,6 +68,7 @@ SIGNATURES = {
     "clove_cuda_launch_count": (C.c_uint64, []),
     "clove_cuda_debug_set": (_i, [C.c_uint32, _i]),
     "clove_cuda_debug_phase_timing": (_i, [_i]),
+    "clove_cuda_debug_trace": (_i, [_vp]),
     "clove_cuda_debug_phase_ms": (_i, [C.POINTER(_f), C.POINTER(_f), C.POINTER(_f)]),
 }
 

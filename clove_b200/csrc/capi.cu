@@ -476,10 +476,13 @@ int clove_cuda_decode_status(void* workspace, void* stream, int* flags) {
     return CLOVE_ERR_INVALID_ARG;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // word 1 of the workspace: the flags the last completed call published
+  // (its combine kernel moves them there from the accumulating word 0)
+  int32_t* last = static_cast<int32_t*>(workspace) + 1;
   int host = 0;
-  cudaError_t e = cudaMemcpyAsync(&host, workspace, sizeof(int), cudaMemcpyDeviceToHost, s);
+  cudaError_t e = cudaMemcpyAsync(&host, last, sizeof(int), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-  if (e == cudaSuccess) e = cudaMemsetAsync(workspace, 0, sizeof(int), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(last, 0, sizeof(int), s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return cuda_fail("decode_status", e);
   if (flags) *flags = host;
@@ -508,6 +511,11 @@ int clove_cuda_debug_phase_timing(int enable) {
 
 int clove_cuda_debug_phase_ms(float* plan_ms, float* decode_ms, float* combine_ms) {
   return read_phase_ms(plan_ms, decode_ms, combine_ms);
+}
+
+int clove_cuda_debug_trace(void* buffer) {
+  set_trace_buffer(buffer);
+  return kTrace ? CLOVE_OK : CLOVE_ERR_UNSUPPORTED;
 }
 
 int clove_cuda_debug_set(uint32_t wait_limit, int inject_stall) {

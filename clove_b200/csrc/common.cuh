@@ -199,6 +199,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 // ---------------------------------------------------------------------------
 // kernel parameter blocks
 // ---------------------------------------------------------------------------
+// Floats per softmax state row (acc[D], m, l) in shared scratch and in the
+// partials: padded to a multiple of 4 so rows start 16-byte aligned.
+__host__ __device__ constexpr int state_stride(int head_dim) { return head_dim + 4; }
+
 struct DecodeArgs {
   const void* q;             // [B, Hq, D] pool dtype
   const void* k_new;         // [B, Hkv, D] or null (no append)
@@ -208,52 +212,53 @@ struct DecodeArgs {
   const int32_t* block_tables;
   const int32_t* context_lens;
   float* out;                // [B, Hq, D] f32
-  float* partials;           // [B*Hkv, max_chunks, G, D + 2] f32
-  const int2* items;         // [n_items] (b, chunk)
-  const int32_t* n_items;    // device scalar
-  const int32_t* seq_chunks; // [B] chunks per sequence
-  int32_t* err;              // device check flags
+  float* partials;           // [num_ctas, 2, group, state_stride(D)] f32: a CTA's first / last piece when split
+  int4* desc;                // [num_ctas]: segment at the CTA's range start {b, h, offset, blocks}
+  int32_t* err;              // device check flags raised by this call (accumulated)
+  int32_t* err_last;         // flags of the last completed call (published by the combine)
+  long long* total;          // work W of this call in (segment, block) units (CTA 0 writes it)
   int bt_stride;
   int batch;
   int num_kv_heads;
   int num_blocks;
   int block_size;
-  const int32_t* chunk_blocks;  // device scalar: blocks per work item (set by the plan)
-  int32_t* unit_counter;        // work-claim counter (zeroed by the plan)
-  const int32_t* multi;         // sequences split into several chunks (plan)
-  const int32_t* n_multi;
-  int max_chunks;            // chunks per sequence, upper bound
+  int num_ctas;              // P: decode CTAs (the partition's divisor)
+  int seg_cost;              // alpha: stream positions charged per segment for a piece's fixed cost
   int max_ctx;
   int group;                 // query heads per KV head (runtime, <= template G)
   int append;                // 1: context_lens are pre-append lengths
   int nstage;                // pipeline depth (a multiple of ncw)
   int ncw;                   // consumer warps that take stages (<= the kernel's NCW)
   int stage_blocks;          // blocks per pipeline stage (1..4)
+  int nscr;                  // merge scratch buffers (1 or 2)
   uint32_t wait_limit;       // polls before a pipeline wait is declared stuck
-  int inject_stall;          // test hook: the first stage of unit 0 is never filled
+  int inject_stall;          // test hook: the first stage of each CTA's first piece is never filled
   float qscale;              // scale * log2(e)
+  unsigned long long* trace; // timeline buffer (trace builds only; null otherwise)
 };
 
-struct PlanArgs {
-  const int32_t* context_lens;
-  int2* items;
-  int32_t* n_items;
-  int32_t* seq_chunks;
-  float* out;
-  int32_t* err;
-  int batch;
-  int num_kv_heads;
-  int row_floats;  // Hq * D: output floats per sequence
-  int block_size;
-  int min_chunk_blocks;      // lower bound on blocks per work item
-  int max_chunk_blocks;      // upper bound (a unit streams at most ~2 MiB of K/V)
-  long long target_units;    // work units the chunk size aims for
-  int32_t* chunk_blocks;     // out: blocks per work item chosen for this call
-  int32_t* unit_counter;     // zeroed: the decode kernel's work-claim counter
-  int32_t* multi;            // out: sequences split into several chunks
-  int32_t* n_multi;          // out: their count
-  int max_ctx;
-  int append;
-};
+// Timeline tracing for measurement builds (compiled with -DCLOVE_TRACE; the
+// product build contains none of it).  u64 slots of the buffer:
+//   [0] plan start, [1] plan end, [2] first combine CTA start, [3] last
+//   combine CTA end; [kTraceCta + 4 cta + k]: decode CTA k = 0 entry, 1 past
+//   griddepcontrol.wait, 2 producer done, 3 last consumer done;
+//   [kTraceUnit + 3 u + k]: piece u = 16 cta + (piece index within the
+//   CTA, < 16) k = 0 posted, 1 merged, 2 (cta << 32) | blocks.  Times from
+//   %globaltimer (ns).
+#ifdef CLOVE_TRACE
+constexpr bool kTrace = true;
+#else
+constexpr bool kTrace = false;
+#endif
+constexpr int kTraceCta = 16;
+constexpr int kTraceMaxCta = 4096;
+constexpr int kTraceUnit = kTraceCta + 4 * kTraceMaxCta;
+constexpr int kTraceMaxUnit = 65536;
+
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 }  // namespace clove

@@ -1,31 +1,29 @@
 // PagedAttention decode for sm_100a.
 //
-// Work decomposition.  A work unit is (sequence b, context chunk c, KV head
-// h): `chunk_blocks` consecutive logical blocks of one sequence, for all the
-// query heads that share KV head h (the GQA group).  K/V of a unit are read
-// from HBM exactly once; every query head of the group consumes them from
-// shared memory.
+// Work decomposition (decode_common.cuh): the call's KV reads form one stream
+// of (sequence, KV head) segments, each as many blocks long as its sequence;
+// decode CTA c of P streams positions [c W / P, (c + 1) W / P), so every CTA
+// reads the same number of K/V blocks.  A piece (the part of one segment in
+// one CTA's range) is consumed for all query heads of the GQA group, so K/V
+// are read from HBM exactly once.
 //
-// Two launches per call:
-//   plan_kernel     1 CTA: per-sequence chunk counts, a compact list of
-//                   (b, c) items, counter reset, zero rows for empty
-//                   sequences, context-length checks.
-//   decode kernel   persistent: gridDim = SMs x resident CTAs, each CTA walks
-//                   units u = blockIdx.x + k*gridDim.x.  One producer warp
-//                   streams K/V tiles (one block of one head = a
-//                   [block_size, head_dim] box) into a shared-memory ring with
-//                   3-D bulk tensor copies (TMA) and mbarriers; consumer warps
-//                   compute QK^T, an fp32 online softmax and P.V.  A sequence
-//                   split into several chunks writes per-chunk partials
-//                   (m, l, acc); the CTA that finishes the last chunk of
-//                   (b, h) — detected with an atomic counter, no waiting —
-//                   merges them with a log-sum-exp combine and writes the
-//                   output.  No inter-CTA spin-waits exist.
+// Two launches per call, chained with programmatic dependent launch:
+//   decode kernel   persistent, P = SMs x resident CTAs.  Every CTA first
+//                   computes the partition itself (two block-wide scans of
+//                   context_lens), then one producer warp streams K/V tiles
+//                   (one block of one head = a [block_size, head_dim] box)
+//                   into a shared-memory ring with bulk tensor copies (TMA)
+//                   and mbarriers, and consumer warps compute QK^T, an fp32
+//                   online softmax and P.V.  Whole segments write their
+//                   output rows; a segment split by a CTA boundary leaves a
+//                   partial (m, l, acc) per piece.
+//   combine kernel  merges the partials of split segments with a
+//                   log-sum-exp combine, and publishes the call's check flags.
 //
-// With append (fused reshape-and-cache), the CTA that owns the last chunk of
-// (b, h) writes the new token's K/V row of head h into its slot before it
-// issues the tile copies of that chunk (ordered with a proxy fence), so the
-// tile it then reads already holds the new token.
+// With append (fused reshape-and-cache), the piece that holds a segment's
+// last block writes the new token's K/V row of that head into its slot before
+// it issues the tile copies (ordered with a proxy fence), so the tile it then
+// reads already holds the new token.
 //
 // Semantics follow the reference's documented op: softmax(q.K^T * scale).V
 // (src/nn/attention.rs:52-69), scale 1/sqrt(head_dim) supplied by the caller
@@ -42,136 +40,6 @@
 #include "mma_decode.cuh"
 
 namespace clove {
-
-// ---------------------------------------------------------------------------
-// plan
-// ---------------------------------------------------------------------------
-constexpr int kPlanThreads = 1024;
-
-constexpr int kPlanBins = 256;
-
-// Block-wide exclusive scan of one int per thread; *total gets the sum.
-__device__ __forceinline__ int block_excl_scan(int n, int* warp_tot, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = n;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) warp_tot[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int w = warp_tot[lane];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += y;
-    }
-    warp_tot[lane] = w;  // inclusive over warps
-  }
-  __syncthreads();
-  const int excl = x - n + (warp > 0 ? warp_tot[warp - 1] : 0);
-  *total = warp_tot[31];
-  __syncthreads();
-  return excl;
-}
-
-// Work list, longest first: every sequence of nbl blocks yields nbl / cb
-// full chunks (listed first, all the same size) and, if nbl % cb != 0, one
-// partial chunk; the partial chunks follow in descending size order (counting
-// sort over kPlanBins size bins).  The decode kernel's CTAs claim units from
-// the front with an atomic counter, so the big units start first and the
-// small ones fill the tail.
-__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanArgs p) {
-  __shared__ int warp_tot[32];
-  __shared__ int hist[kPlanBins];
-  __shared__ int binbase[kPlanBins];
-  __shared__ long long s_blocks;
-  __shared__ int s_full;
-  const int tid = threadIdx.x, lane = tid & 31;
-  // Let the decode kernel launch now: it sets up its barriers and then waits
-  // (griddepcontrol.wait) for this grid's results.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  // Context lengths of this thread's first sequence stay in registers; only
-  // batches beyond kPlanThreads sequences re-read the rest.
-  const int b0 = tid;
-  const int L0 = b0 < p.batch ? clamp_ctx(p.context_lens, b0, p.max_ctx, p.append) : 0;
-  if (tid == 0) {
-    s_blocks = 0;
-    s_full = 0;
-    *p.err = 0;            // flags report the most recent call only
-    *p.unit_counter = 0;   // the decode kernel's work-claim counter
-    *p.n_multi = 0;
-  }
-  for (int i = tid; i < kPlanBins; i += kPlanThreads) hist[i] = 0;
-  __syncthreads();
-  auto len_of = [&](int b) { return b == b0 ? L0 : clamp_ctx(p.context_lens, b, p.max_ctx, p.append); };
-  // Chunk size from the actual work: total (block, KV head) pairs spread
-  // over ~target_units work items, capped at max_chunk_blocks, never below
-  // min_chunk_blocks.
-  {
-    long long mine = 0;
-    for (int b = tid; b < p.batch; b += kPlanThreads) mine += (len_of(b) + p.block_size - 1) / p.block_size;
-    for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
-    if (lane == 0 && mine) atomicAdd(reinterpret_cast<unsigned long long*>(&s_blocks), (unsigned long long)mine);
-  }
-  __syncthreads();
-  const long long want = (s_blocks * p.num_kv_heads + p.target_units - 1) / p.target_units;
-  const int cb = (int)max((long long)p.min_chunk_blocks, min((long long)p.max_chunk_blocks, want));
-  if (tid == 0) *p.chunk_blocks = cb;
-
-  // pass 1: per-sequence bookkeeping, full chunks, partial-size histogram
-  for (int base = 0; base < p.batch; base += kPlanThreads) {
-    const int b = base + tid;
-    int nfull = 0;
-    if (b < p.batch) {
-      const int raw = __ldg(p.context_lens + b);
-      const int L = len_of(b);
-      if (raw != L - p.append) atomicOr(p.err, CLOVE_FLAG_CTX_RANGE);
-      const int nbl = (L + p.block_size - 1) / p.block_size;
-      nfull = nbl / cb;
-      const int rem = nbl - nfull * cb;
-      p.seq_chunks[b] = nfull + (rem > 0);
-      if (nfull + (rem > 0) > 1) p.multi[atomicAdd(p.n_multi, 1)] = b;
-      if (rem > 0) atomicAdd(&hist[(rem - 1) * kPlanBins / cb], 1);
-      if (L == 0) {
-        float* row = p.out + (size_t)b * p.row_floats;
-        for (int i = 0; i < p.row_floats; ++i) row[i] = 0.f;
-      }
-    }
-    int tot;
-    const int excl = block_excl_scan(nfull, warp_tot, &tot);
-    for (int c = 0; c < nfull; ++c) p.items[s_full + excl + c] = make_int2(b, c);
-    __syncthreads();
-    if (tid == 0) s_full += tot;
-    __syncthreads();
-  }
-  // partial chunks: bases per size bin, largest bin first (parallel scan over
-  // the bins in descending order)
-  {
-    const int bin = kPlanBins - 1 - tid;
-    const int cnt = tid < kPlanBins ? hist[bin] : 0;
-    int tot;
-    const int excl = block_excl_scan(cnt, warp_tot, &tot);
-    if (tid < kPlanBins) {
-      binbase[bin] = s_full + excl;
-      hist[bin] = 0;  // reused as the per-bin cursor
-    }
-    if (tid == 0) *p.n_items = s_full + tot;
-  }
-  __syncthreads();
-  for (int b = tid; b < p.batch; b += kPlanThreads) {
-    const int L = len_of(b);
-    const int nbl = (L + p.block_size - 1) / p.block_size;
-    const int nfull = nbl / cb;
-    const int rem = nbl - nfull * cb;
-    if (rem > 0) {
-      const int bin = (rem - 1) * kPlanBins / cb;
-      p.items[binbase[bin] + atomicAdd(&hist[bin], 1)] = make_int2(b, nfull);
-    }
-  }
-}
 
 // ---------------------------------------------------------------------------
 // the CUDA-core decode kernel
@@ -199,7 +67,6 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
     paged_decode_simt_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                              const DecodeArgs a) {
   constexpr int E = D / 32;
-  constexpr int NCT = NCW * 32;
   constexpr int EPC = 16 / (int)sizeof(T);  // elements per 16-byte chunk
   const int bs = a.block_size;
   const int sb = a.stage_blocks;
@@ -214,14 +81,22 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const SmemPlan sp = smem_plan(bs, D, (int)sizeof(T), sb, a.nstage,
-                                NCW * G * (D + 2) * (int)sizeof(float), G * D * (int)sizeof(T));
+                                NCW * group * state_stride(D) * (int)sizeof(float), group * D * (int)sizeof(T),
+                                a.nscr);
   const SmemPtrs sm = smem_ptrs(smem, sp, a.nstage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0 && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 4 * blockIdx.x] = gtime();
+  }
   init_barriers(sm, a.nstage, NCW);
-  const int n_units = *a.n_items * a.num_kv_heads;
+  __shared__ WalkStart walk;
+  partition_prologue<D>(a, &walk);
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0 && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 4 * blockIdx.x + 1] = gtime();
+  }
 
   if (warp == 0) {
-    produce<T, D, 1>(a, &tm_k, &tm_v, sm, sp, sb, n_units);
+    produce<T, D, 1>(a, &tm_k, &tm_v, sm, sp, sb, walk);
     return;
   }
 
@@ -263,7 +138,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       }
       const T* Ks = reinterpret_cast<const T*>(sm.ring + (size_t)slot * sp.stage_bytes);
       const T* Vs = reinterpret_cast<const T*>(sm.ring + (size_t)slot * sp.stage_bytes + sb * sp.tile_stride);
-      const int ntok = min(TT, x.L - (x.blk0 + j * sb) * bs);
+      // tokens of this stage: up to the piece's end (a piece may end inside
+      // a stage of sb blocks, before its sequence does) and the sequence's
+      const int ntok = min(TT, min((x.blk0 + x.nblk) * bs, x.L) - (x.blk0 + j * sb) * bs);
       for (int p0 = 0; p0 < ntok; p0 += P) {
         const int tk = p0 + tk_l;
         // ---- scores ----
@@ -328,18 +205,19 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
     if (aborted) return;  // the abort flag is up; every other warp leaves at its next wait
     gbase += x.nstages;
 
-    // ---- publish this warp's state (double-buffered scratch), hand off ----
-    const int sbuf = n_done & 1;
-    if (!wait_or_abort(a, sm, &sm.scr_empty[sbuf], ((uint32_t)(n_done >> 1) & 1u) ^ 1u)) return;
-    float* my_scr = sm.scratch + sbuf * sm.scratch_floats + (size_t)cw * G * (D + 2);
+    // ---- publish this warp's state (rows < group) into scratch, hand off ----
+    const int sbuf = n_done % a.nscr;
+    if (!wait_or_abort(a, sm, &sm.scr_empty[sbuf], ((uint32_t)(n_done / a.nscr) & 1u) ^ 1u)) return;
+    float* my_scr = sm.scratch + sbuf * sm.scratch_floats + (size_t)cw * group * state_stride(D);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
+      if (g >= group) break;  // the scratch holds `group` rows per warp
       const float lsum = warp_sum(l[g]);
 #pragma unroll
-      for (int e = 0; e < E; ++e) my_scr[g * (D + 2) + lane * E + e] = acc[g][e];
+      for (int e = 0; e < E; ++e) my_scr[g * state_stride(D) + lane * E + e] = acc[g][e];
       if (lane == 0) {
-        my_scr[g * (D + 2) + D] = m[g];
-        my_scr[g * (D + 2) + D + 1] = lsum;
+        my_scr[g * state_stride(D) + D] = m[g];
+        my_scr[g * state_stride(D) + D + 1] = lsum;
       }
     }
     hand_off<D, G, NCW>(a, sm, us, sbuf, uk, lane);
@@ -349,88 +227,150 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       uphase ^= 1;
     }
   }
+  if constexpr (kTrace) {
+    if (a.trace && lane == 0 && blockIdx.x < kTraceMaxCta)
+      atomicMax(a.trace + kTraceCta + 4 * blockIdx.x + 3, gtime());
+  }
 }
 
 // ---------------------------------------------------------------------------
-// split-K combine
+// combine
 // ---------------------------------------------------------------------------
-// One CTA per (sequence, query head): for a sequence the decode split into
-// several chunks, merge the chunk states (m, l, acc) of the partials with a
-// log-sum-exp combine and write the output row.  Sequences in one chunk were
-// finished by the decode kernel; their CTAs exit at once.  Launched as a
-// programmatic dependent of the decode kernel.
+// Segments split by CTA boundaries: segment s is split iff some boundary
+// range_begin(c), 0 < c < P, falls strictly inside it; its pieces are those
+// of CTAs cta_of(S) .. cta_of(S + len - 1).  The CTA whose range starts at
+// (or before) S keeps its piece in partial slot 1 (its last piece) unless its
+// range starts exactly at S (slot 0); every later CTA keeps it in slot 0 (its
+// first piece).  Combine CTAs stride over the boundaries c and merge the
+// segment whose first interior boundary is c.
 constexpr int kCombineThreads = 128;
-constexpr int kCombineMaxChunks = 2048;  // chunk weights staged in shared memory
+constexpr int kCombineMaxPieces = 1024;  // >= P (decode CTAs) - checked on the host
 
-// Merge the chunks of (sequence b, query head hq): M = max m_c,
-// w_c = 2^(m_c - M), out = sum_c w_c acc_c / sum_c w_c l_c.  All threads of
-// the CTA take part; ends with a CTA barrier so the shared arrays can be
-// reused.
-__device__ void combine_one(const DecodeArgs& a, int D, int b, int hq, float* w, float* red, float* bcast) {
+// States staged in shared memory per round (8 rows of head_dim + 4 floats
+// each; fewer for head_dim 256 to stay within static shared memory); more
+// pieces are merged in rounds, the running state taking one entry of the
+// next round.
+template <int D>
+__host__ __device__ constexpr int combine_stage() { return D > 128 ? 4 : 8; }
+constexpr int kWtsL = 64, kWtsM = 72;  // wts[]: row sums and maxima after the per-state weights
+
+// Merge the np partial states listed in pieces[] (partial slot indices
+// c * 2 + slot) of segment (b, h) and write its output rows.  All threads of
+// the CTA take part.  Each round stages up to kCombineStage states in shared
+// memory with one batch of independent 16-byte loads, then per row g:
+// M = max_i m_i, w_i = 2^(m_i - M), L = sum_i w_i l_i, acc = sum_i w_i acc_i.
+template <int D>
+__device__ void combine_segment(const DecodeArgs& a, int b, int h, const int* pieces, int np, float* st,
+                                float* wts, float* run) {
+  constexpr int S = state_stride(D);
   const int group = a.group;
   const int Hq = a.num_kv_heads * group;
-  const int h = hq / group, g = hq - h * group;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const size_t cstride = (size_t)group * (D + 2);  // floats between consecutive chunks
-  const float* base = a.partials + (((size_t)b * a.num_kv_heads + h) * a.max_chunks * group + g) * (D + 2);
-  const int nc = min(a.seq_chunks[b], kCombineMaxChunks);  // decode_layout keeps it within bounds
-  float mx = -INFINITY;
-  for (int c = tid; c < nc; c += kCombineThreads) mx = fmaxf(mx, base[c * cstride + D]);
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) red[warp] = mx;
-  __syncthreads();
-  if (tid == 0) {
-    float m = red[0];
-    for (int i = 1; i < kCombineThreads / 32; ++i) m = fmaxf(m, red[i]);
-    *bcast = m;
-  }
-  __syncthreads();
-  const float M = *bcast;
-  float ls = 0.f;
-  for (int c = tid; c < nc; c += kCombineThreads) {
-    const float wc = exp2f(base[c * cstride + D] - M);
-    w[c] = wc;
-    ls = fmaf(wc, base[c * cstride + D + 1], ls);
-  }
-  for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
-  __syncthreads();
-  if (lane == 0) red[warp] = ls;
-  __syncthreads();
-  if (tid == 0) {
-    float t = 0.f;
-    for (int i = 0; i < kCombineThreads / 32; ++i) t += red[i];
-    *bcast = 1.f / t;
-  }
-  __syncthreads();
-  const float inv = *bcast;
-  // loads coalesced over d, independent over c
-  for (int d = tid; d < D; d += kCombineThreads) {
-    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-    int c = 0;
-    for (; c + 4 <= nc; c += 4) {
-      o0 = fmaf(w[c], base[c * cstride + d], o0);
-      o1 = fmaf(w[c + 1], base[(c + 1) * cstride + d], o1);
-      o2 = fmaf(w[c + 2], base[(c + 2) * cstride + d], o2);
-      o3 = fmaf(w[c + 3], base[(c + 3) * cstride + d], o3);
+  const int tid = threadIdx.x;
+  const int row4 = S / 4;  // float4 per state row
+  bool have_run = false;
+  for (int base = 0; base < np;) {
+    const int first = have_run ? 1 : 0;
+    const int n = min(combine_stage<D>() - first, np - base);
+    const int ne = n + first;
+    if (have_run)
+      for (int i = tid; i < group * row4; i += kCombineThreads)
+        reinterpret_cast<float4*>(st)[i] = reinterpret_cast<const float4*>(run)[i];
+    for (int i = tid; i < n * group * row4; i += kCombineThreads) {
+      const int p = i / (group * row4), r = i - p * (group * row4);
+      reinterpret_cast<float4*>(st)[first * group * row4 + i] =
+          __ldcg(reinterpret_cast<const float4*>(a.partials + (size_t)pieces[base + p] * group * S) + r);
     }
-    for (; c < nc; ++c) o0 = fmaf(w[c], base[c * cstride + d], o0);
-    a.out[((size_t)b * Hq + hq) * D + d] = ((o0 + o1) + (o2 + o3)) * inv;
+    __syncthreads();
+    for (int g = tid >> 5; g < group; g += kCombineThreads / 32) {
+      const int lane = tid & 31;
+      float M = -INFINITY;
+      for (int i = lane; i < ne; i += 32) M = fmaxf(M, st[(i * group + g) * S + D]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      float ls = 0.f;
+      for (int i = lane; i < ne; i += 32) {
+        const float mi = st[(i * group + g) * S + D];
+        const float wi = mi == -INFINITY ? 0.f : exp2f(mi - M);
+        wts[i * group + g] = wi;
+        ls = fmaf(wi, st[(i * group + g) * S + D + 1], ls);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+      if (lane == 0) {
+        wts[kWtsL + g] = ls;
+        wts[kWtsM + g] = M;
+      }
+    }
+    __syncthreads();
+    base += n;
+    const bool last_round = base >= np;
+    for (int idx = tid; idx < group * D; idx += kCombineThreads) {
+      const int g = idx / D, d = idx - (idx / D) * D;
+      float o = 0.f;
+      for (int i = 0; i < ne; ++i) o = fmaf(wts[i * group + g], st[(i * group + g) * S + d], o);
+      if (last_round) {
+        a.out[((size_t)b * Hq + (size_t)h * group + g) * D + d] = o / wts[kWtsL + g];
+      } else {
+        run[g * S + d] = o;
+      }
+    }
+    if (!last_round && tid < group) {
+      run[tid * S + D] = wts[kWtsM + tid];
+      run[tid * S + D + 1] = wts[kWtsL + tid];
+    }
+    __syncthreads();
+    have_run = true;
   }
-  __syncthreads();
 }
 
-// Split-K combine: CTAs stride over the (sequence, query head) pairs of the
-// sequences the plan split into several chunks (the others were finished by
-// the decode kernel).  Launched as a programmatic dependent of the decode.
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeArgs a, int head_dim) {
-  __shared__ float w[kCombineMaxChunks];
-  __shared__ float red[kCombineThreads / 32];
-  __shared__ float bcast;
+template <int D>
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeArgs a) {
+  constexpr int S = state_stride(D);
+  __shared__ __align__(16) float st[combine_stage<D>() * 8 * S];
+  __shared__ float wts[kWtsM + 8];
+  __shared__ __align__(16) float run[8 * S];  // running merged state between rounds
+  __shared__ int pieces[kCombineMaxPieces];
+  __shared__ int s_np;
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int Hq = a.num_kv_heads * a.group;
-  const int n_items = *a.n_multi * Hq;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x)
-    combine_one(a, head_dim, a.multi[item / Hq], item - (item / Hq) * Hq, w, red, &bcast);
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0) atomicMin(a.trace + 2, gtime());
+  }
+  // The decode grid has finished: publish this call's check flags and clear
+  // the accumulating word for the next call (whose decode waits for this
+  // grid before it raises anything).
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *a.err_last = *a.err;
+    *a.err = 0;
+  }
+  const long long W = *a.total;
+  const long long P = a.num_ctas;
+  const int alpha = a.seg_cost;
+  for (int c = 1 + blockIdx.x; c < P; c += gridDim.x) {
+    const int4 d = a.desc[c];
+    // empty range, or the boundary does not fall inside the segment's blocks
+    if (d.x < 0 || d.z <= alpha) continue;
+    // segment (d.x, d.y) starts at stream position S0 and is d.w positions
+    // long; it is merged by the iteration of the first boundary inside its
+    // blocks (CTAs with empty ranges may sit between: compare owners)
+    const long long S0 = range_begin(c, W, P) - d.z;
+    const long long c_first = cta_of(S0 + alpha, W, P);
+    if (cta_of(range_begin(c, W, P) - 1, W, P) != c_first) continue;
+    const long long c_last = cta_of(S0 + d.w - 1, W, P);
+    if (threadIdx.x == 0) {
+      int np = 0;
+      for (long long k = c_first; k <= c_last && np < kCombineMaxPieces; ++k) {
+        if (range_begin(k, W, P) == range_begin(k + 1, W, P)) continue;  // an empty range holds no piece
+        const int slot = (k == c_first && range_begin(k, W, P) < S0) ? 1 : 0;
+        pieces[np++] = (int)(k * 2 + slot);
+      }
+      s_np = np;
+    }
+    __syncthreads();
+    combine_segment<D>(a, d.x, d.y, pieces, s_np, st, wts, run);
+  }
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0) atomicMax(a.trace + 3, gtime());
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -439,84 +379,120 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeAr
 constexpr int kNCW = 4;          // consumer warps of the CUDA-core kernel
 constexpr int kRingTarget = 96 * 1024;
 
-// Smallest work item: 256 tokens (a chunk shorter than that spends more on
-// its epilogue than on streaming).  The plan kernel picks the actual chunk
-// size per call from the total work; this bound sizes the workspace.
-static int min_chunk_blocks(int block_size) { return (256 + block_size - 1) / block_size; }
-
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Stream positions charged per segment for the fixed cost of starting a
+// piece (query load, the consumer warps' state hand-off and merge): 40 KB
+// worth of blocks (one position = the K and V [block_size, head_dim] tiles of
+// one head).  Measured by sweeping it: the best steps came at 40-48 KB on
+// c3 (8 KB blocks, alpha 5) and c5 (16 KB blocks, alpha 3).
+// CLOVE_SEG_COST overrides it (for measurement sweeps).
+static int segment_cost(const clove_pool& pool) {
+  static const int env = [] {
+    const char* v = std::getenv("CLOVE_SEG_COST");
+    return v ? std::max(0, std::atoi(v)) : -1;
+  }();
+  if (env >= 0) return env;
+  const int block_bytes = 2 * pool.block_size * pool.head_dim * pool.elem_bytes;
+  return std::max(1, (40 * 1024 + block_bytes - 1) / block_bytes);
+}
+
 DecodeLayout decode_layout(const clove_pool& pool, int batch, int num_q_heads, int max_ctx) {
+  (void)batch;
+  (void)max_ctx;
   DecodeLayout L;
-  const int hkv = pool.num_kv_heads;
-  const int group = num_q_heads / hkv;
-  const int max_blocks = (max_ctx + pool.block_size - 1) / pool.block_size;
-  // Smallest chunk: 256 tokens, and few enough chunks per sequence for the
-  // combine kernel's shared-memory weights.
-  L.chunk_blocks = max(min_chunk_blocks(pool.block_size), (max_blocks + kCombineMaxChunks - 1) / kCombineMaxChunks);
-  L.max_chunks = max_blocks <= 0 ? 1 : (max_blocks + L.chunk_blocks - 1) / L.chunk_blocks;
+  const int group = num_q_heads / pool.num_kv_heads;
+  L.max_ctas = pool.num_sms * kMaxCtasPerSm;
   size_t off = 0;
-  L.off_err = off;
+  L.off_err = off;  // [0] flags of this call, [1] flags of the last call, [4..5] W
   off += 256;
-  L.off_nitems = off;
-  off += 256;
-  L.off_items = off;
-  off = align256(off + sizeof(int2) * (size_t)batch * L.max_chunks);
-  L.off_seq_chunks = off;
-  off = align256(off + sizeof(int32_t) * (size_t)batch);
-  L.off_multi = off;
-  off = align256(off + sizeof(int32_t) * (size_t)batch);
+  L.off_desc = off;
+  off = align256(off + sizeof(int4) * (size_t)L.max_ctas);
   L.off_partials = off;
-  // Partials are only written when a sequence spans more than one chunk.
-  if (L.max_chunks > 1)
-    off = align256(off + sizeof(float) * (size_t)batch * hkv * L.max_chunks * group * (pool.head_dim + 2));
+  off = align256(off + sizeof(float) * (size_t)L.max_ctas * 2 * group * state_stride(pool.head_dim));
   L.total = off;
   return L;
 }
 
+// Launch configuration of one decode kernel instance for one pool shape,
+// worked out once (function attributes and the occupancy query are not free
+// on the host).
+struct KernelCfg {
+  int ok = 0;
+  int nstage = 0, ncw = 0, smem = 0, ctas = 0;
+};
+
 template <typename T, int D, int G>
-static int run_simt(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
+static KernelCfg simt_cfg(const clove_pool& pool, int group) {
+  static std::mutex mu;
+  static std::unordered_map<long long, KernelCfg> cache;
+  const long long key = ((long long)pool.device << 32) | ((long long)pool.block_size << 8) | group;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  KernelCfg c;
   auto kern = paged_decode_simt_kernel<T, D, G, kNCW>;
   const int bs = pool.block_size;
   const int sb = bs >= 16 ? 1 : 16 / bs;
-  a.stage_blocks = sb;
-  const int scratch = kNCW * G * (D + 2) * 4;
-  const int qb = G * D * (int)sizeof(T);
-  SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb);
+  const int scratch = kNCW * group * state_stride(D) * 4;
+  const int qb = group * D * (int)sizeof(T);
+  SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb, 2);
   // nstage: a multiple of the number of consumer warps that take stages (see
   // the kernel); large tiles use fewer of them.
   int ncw = kNCW;
   int nstage = (kRingTarget / sp.stage_bytes) / ncw * ncw;
   if (nstage < ncw) nstage = ncw;
   if (nstage > 4 * ncw) nstage = 4 * ncw;
-  sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);
+  sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb, 2);
   while (sp.total > 200 * 1024 && nstage > 1) {
     if (nstage > ncw) {
       nstage -= ncw;
     } else {
       ncw = --nstage;
     }
-    sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);
+    sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb, 2);
   }
-  a.ncw = ncw;
   if (sp.total > 227 * 1024) {
     set_last_error("paged_decode: block_size %d x head_dim %d tile does not fit shared memory", bs, D);
-    return CLOVE_ERR_UNSUPPORTED;
+    return c;  // not cached: the error text is set on every call
   }
-  a.nstage = nstage;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sp.total);
-  if (e != cudaSuccess) {
-    set_last_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    return CLOVE_ERR_CUDA;
+  // The attribute belongs to the kernel, not to this block size: only raise
+  // it, so configurations cached for other block sizes stay launchable.
+  static int attr_smem = 0;
+  if (sp.total > attr_smem) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sp.total) != cudaSuccess) {
+      set_last_error("cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError()));
+      return c;
+    }
+    attr_smem = sp.total;
   }
   int occ = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, (kNCW + 1) * 32, sp.total);
-  if (e != cudaSuccess || occ < 1) occ = 1;
-  long long units_max = (long long)a.batch * a.max_chunks * a.num_kv_heads;
-  long long grid = (long long)pool.num_sms * occ;
-  if (grid > units_max) grid = units_max;
-  if (grid < 1) grid = 1;
-  e = launch_dependent(kern, (unsigned)grid, (kNCW + 1) * 32, sp.total, stream, pool.tm_k, pool.tm_v, a);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, (kNCW + 1) * 32, sp.total) != cudaSuccess ||
+      occ < 1) {
+    cudaGetLastError();
+    occ = 1;
+  }
+  c.ok = 1;
+  c.nstage = nstage;
+  c.ncw = ncw;
+  c.smem = sp.total;
+  c.ctas = pool.num_sms * std::min(occ, kMaxCtasPerSm);
+  cache[key] = c;
+  return c;
+}
+
+template <typename T, int D, int G>
+static int run_simt(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
+  const KernelCfg c = simt_cfg<T, D, G>(pool, a.group);
+  if (!c.ok) return CLOVE_ERR_UNSUPPORTED;
+  const int bs = pool.block_size;
+  a.stage_blocks = bs >= 16 ? 1 : 16 / bs;
+  a.nscr = 2;
+  a.nstage = c.nstage;
+  a.ncw = c.ncw;
+  a.num_ctas = c.ctas;
+  cudaError_t e = launch_dependent(paged_decode_simt_kernel<T, D, G, kNCW>, (unsigned)c.ctas, (kNCW + 1) * 32,
+                                   c.smem, stream, pool.tm_k, pool.tm_v, a);
   if (e != cudaSuccess) {
     set_last_error("paged_decode launch: %s", cudaGetErrorString(e));
     return CLOVE_ERR_CUDA;
@@ -590,6 +566,9 @@ static void phase_mark(int i, cudaStream_t stream) {
 
 void set_phase_timing(int on) { g_phase_timing.store(on ? 1 : 0); }
 
+static std::atomic<unsigned long long*> g_trace{nullptr};
+void set_trace_buffer(void* buf) { g_trace.store(static_cast<unsigned long long*>(buf)); }
+
 int read_phase_ms(float* plan_ms, float* decode_ms, float* combine_ms) {
   std::lock_guard<std::mutex> lk(g_phase_mu);
   if (!g_phase_recorded) {
@@ -618,38 +597,6 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   unsigned char* ws = static_cast<unsigned char*>(call.workspace);
   const int append = call.k_new != nullptr ? 1 : 0;
 
-  PlanArgs p;
-  p.context_lens = call.context_lens;
-  p.items = reinterpret_cast<int2*>(ws + L.off_items);
-  p.n_items = reinterpret_cast<int32_t*>(ws + L.off_nitems);
-  p.seq_chunks = reinterpret_cast<int32_t*>(ws + L.off_seq_chunks);
-  p.out = call.out;
-  p.err = reinterpret_cast<int32_t*>(ws + L.off_err);
-  p.batch = call.batch;
-  p.num_kv_heads = pool.num_kv_heads;
-  p.row_floats = call.num_q_heads * pool.head_dim;
-  p.block_size = pool.block_size;
-  p.min_chunk_blocks = L.chunk_blocks;
-  // ~2 units per resident CTA, and no unit above ~2 MiB of K/V, so the tail
-  // (the last units still streaming) stays short (measured on c2-c5).
-  p.target_units = (long long)pool.num_sms * 4;
-  p.max_chunk_blocks = (int)((2u << 20) / (2u * pool.block_size * pool.head_dim * pool.elem_bytes));
-  p.chunk_blocks = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 1;
-  p.unit_counter = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 2;
-  p.n_multi = reinterpret_cast<int32_t*>(ws + L.off_nitems) + 3;
-  p.multi = reinterpret_cast<int32_t*>(ws + L.off_multi);
-  p.max_ctx = call.max_ctx;
-  p.append = append;
-  phase_mark(0, stream);
-  plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    set_last_error("plan launch: %s", cudaGetErrorString(e));
-    return CLOVE_ERR_CUDA;
-  }
-  count_launches(1);
-  phase_mark(1, stream);
-
   DecodeArgs a;
   a.q = call.q;
   a.k_new = call.k_new;
@@ -660,29 +607,31 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
   a.context_lens = call.context_lens;
   a.out = call.out;
   a.partials = reinterpret_cast<float*>(ws + L.off_partials);
-  a.items = p.items;
-  a.n_items = p.n_items;
-  a.seq_chunks = p.seq_chunks;
-  a.err = p.err;
+  a.desc = reinterpret_cast<int4*>(ws + L.off_desc);
+  a.err = reinterpret_cast<int32_t*>(ws + L.off_err);
+  a.err_last = a.err + 1;
+  a.total = reinterpret_cast<long long*>(ws + L.off_err + 16);
   a.bt_stride = call.bt_stride;
   a.batch = call.batch;
   a.num_kv_heads = pool.num_kv_heads;
   a.num_blocks = pool.num_blocks;
   a.block_size = pool.block_size;
-  a.chunk_blocks = p.chunk_blocks;
-  a.unit_counter = p.unit_counter;
-  a.multi = p.multi;
-  a.n_multi = p.n_multi;
-  a.max_chunks = L.max_chunks;
+  a.num_ctas = 1;
+  a.seg_cost = segment_cost(pool);
   a.max_ctx = call.max_ctx;
   a.group = call.num_q_heads / pool.num_kv_heads;
   a.append = append;
   a.nstage = 2;
   a.ncw = 1;
+  a.stage_blocks = 1;
+  a.nscr = 2;
   a.wait_limit = debug_wait_limit();
   a.inject_stall = debug_inject_stall();
   a.qscale = call.scale * kLog2e;
+  a.trace = kTrace ? g_trace.load() : nullptr;
 
+  phase_mark(0, stream);
+  phase_mark(1, stream);  // no planning launch: the plan phase is empty
   int rc;
   switch (pool.dtype) {
     case CLOVE_DTYPE_F32: rc = dispatch_dim<float>(pool, a, stream); break;
@@ -693,16 +642,17 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
       return CLOVE_ERR_UNSUPPORTED;
   }
   if (rc != CLOVE_OK) return rc;
-  phase_mark(2, stream);
-  if (L.max_chunks <= 1) {
-    phase_mark(3, stream);
-    return rc;
+  if (a.num_ctas > L.max_ctas || a.num_ctas > kCombineMaxPieces) {
+    // cannot happen with the occupancy cap; guards the workspace bound
+    set_last_error("paged_decode: %d CTAs exceed the workspace bound %d", a.num_ctas, L.max_ctas);
+    return CLOVE_ERR_UNSUPPORTED;
   }
-  // Split-K combine for the sequences the plan split into several chunks.
+  phase_mark(2, stream);
+  // Combine (always: it also publishes the call's check flags).
   {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::min<long long>((long long)call.batch * call.num_q_heads,
-                                                     (long long)pool.num_sms * 8));
+    // one CTA per boundary between decode CTAs; most find no segment to merge
+    cfg.gridDim = dim3((unsigned)std::max(1, std::min(a.num_ctas - 1, kCombineMaxPieces)));
     cfg.blockDim = dim3(kCombineThreads);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -710,7 +660,12 @@ int launch_decode(const clove_pool& pool, const DecodeCall& call, cudaStream_t s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, combine_kernel, a, pool.head_dim);
+    cudaError_t e;
+    switch (pool.head_dim) {
+      case 64: e = cudaLaunchKernelEx(&cfg, combine_kernel<64>, a); break;
+      case 128: e = cudaLaunchKernelEx(&cfg, combine_kernel<128>, a); break;
+      default: e = cudaLaunchKernelEx(&cfg, combine_kernel<256>, a); break;
+    }
     if (e != cudaSuccess) {
       set_last_error("combine launch: %s", cudaGetErrorString(e));
       return CLOVE_ERR_CUDA;

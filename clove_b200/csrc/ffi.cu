@@ -287,7 +287,8 @@ CTensor clove_paged_attention(CTensor q, CTensor k, CTensor v, CTensor kv, CTens
       if (c.workspace) cudaFreeAsync(c.workspace, 0);
       c.workspace = nullptr;
       c.workspace_bytes = 0;
-      if (cudaMallocAsync(&c.workspace, round_cap(need), 0) == cudaSuccess) {
+      if (cudaMallocAsync(&c.workspace, round_cap(need), 0) == cudaSuccess &&
+          cudaMemsetAsync(c.workspace, 0, round_cap(need), 0) == cudaSuccess) {  // decode scratch starts zeroed
         c.workspace_bytes = round_cap(need);
       } else {
         c.workspace = nullptr;
@@ -316,7 +317,9 @@ CTensor clove_paged_attention(CTensor q, CTensor k, CTensor v, CTensor kv, CTens
   // op is synchronous and aborts on bad input; here the call waits for the
   // decode and returns NULL with the flags in the error text instead of a
   // silently clamped result.
-  if (cudaMemcpyAsync(flags_host, ws, sizeof(int32_t), cudaMemcpyDeviceToHost, 0) != cudaSuccess ||
+  // (word 1 of the scratch: the flags of the call that just completed)
+  if (cudaMemcpyAsync(flags_host, static_cast<int32_t*>(ws) + 1, sizeof(int32_t), cudaMemcpyDeviceToHost, 0) !=
+          cudaSuccess ||
       cudaStreamSynchronize(0) != cudaSuccess) {
     clove_tensor_free(out);
     set_last_error("paged_attention: %s", cudaGetErrorString(cudaGetLastError()));

@@ -36,11 +36,16 @@ struct clove_pool {
 
 namespace clove {
 
+// Decode CTAs per SM are capped here; the workspace holds per-CTA state for
+// num_sms * kMaxCtasPerSm CTAs.
+constexpr int kMaxCtasPerSm = 4;
+
 // Workspace carve-up for one decode call; offsets in bytes from the base.
+// It does not depend on the batch or the context lengths: the partition
+// leaves at most two partial states per decode CTA.
 struct DecodeLayout {
-  int chunk_blocks;  // the smallest chunk the plan may choose
-  int max_chunks;    // chunks per sequence at that size (workspace bound)
-  size_t off_err, off_nitems, off_items, off_seq_chunks, off_multi, off_partials;
+  int max_ctas;
+  size_t off_err, off_desc, off_partials;
   size_t total;
 };
 
@@ -92,6 +97,7 @@ cudaError_t launch_dependent(Kern kern, unsigned grid, unsigned threads, size_t 
   return cudaLaunchKernelEx(&cfg, kern, tk, tv, a);
 }
 
+size_t prefill_mma_scratch_bytes(int num_tokens);
 int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                        const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
                        int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);
@@ -107,5 +113,6 @@ uint32_t debug_wait_limit();
 int debug_inject_stall();
 void set_phase_timing(int on);  // decode_kernels.cu
 int read_phase_ms(float* plan_ms, float* decode_ms, float* combine_ms);
+void set_trace_buffer(void* buf);  // decode_kernels.cu
 
 }  // namespace clove

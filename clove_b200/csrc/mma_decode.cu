@@ -19,6 +19,10 @@
 //
 // Pipeline, work units, ring-slot ownership and the epilogue are those of
 // the CUDA-core kernel (decode_common.cuh).
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
 #include "common.cuh"
 #include "decode_common.cuh"
 #include "host.h"
@@ -45,25 +49,30 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
   constexpr int G = 8;              // rows of the per-KV-head query tile that can be real
   constexpr int KS = D / 16;        // k-steps of QK^T
   constexpr int NT = D / 8;         // n-tiles of P.V
-  constexpr int NCT = NCW * 32;
   const int bs = a.block_size;
   const int sb = a.stage_blocks;
   const int TT = sb * bs;
   const int group = a.group;
-  const int Hq = a.num_kv_heads * group;
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const SmemPlan sp = smem_plan(bs, D, (int)sizeof(T), sb, a.nstage, NCW * G * (D + 2) * (int)sizeof(float),
-                                G * D * (int)sizeof(T));
+  const SmemPlan sp = smem_plan(bs, D, (int)sizeof(T), sb, a.nstage, NCW * group * state_stride(D) * (int)sizeof(float),
+                                group * D * (int)sizeof(T), a.nscr);
   const SmemPtrs sm = smem_ptrs(smem, sp, a.nstage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0 && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 4 * blockIdx.x] = gtime();
+  }
   init_barriers(sm, a.nstage, NCW);
-  const int n_units = *a.n_items * a.num_kv_heads;
+  __shared__ WalkStart walk;
+  partition_prologue<D>(a, &walk);
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0 && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 4 * blockIdx.x + 1] = gtime();
+  }
 
   if (warp == 0) {
-    produce<T, D, 2>(a, &tm_k, &tm_v, sm, sp, sb, n_units);
+    produce<T, D, 2>(a, &tm_k, &tm_v, sm, sp, sb, walk);
     return;
   }
 
@@ -115,7 +124,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       }
       unsigned char* kst = sm.ring + (size_t)slot * sp.stage_bytes;
       unsigned char* vst = kst + sb * sp.tile_stride;
-      const int ntok = min(TT, x.L - (x.blk0 + j * sb) * bs);
+      // tokens of this stage: up to the piece's end (a piece may end inside
+      // a stage of sb blocks, before its sequence does) and the sequence's
+      const int ntok = min(TT, min((x.blk0 + x.nblk) * bs, x.L) - (x.blk0 + j * sb) * bs);
       if (ntok < TT) {
         // Rows past the context may hold any bits (even NaN patterns); P is
         // zero there but 0 * NaN is NaN inside the MMA, so clear those V rows.
@@ -220,18 +231,18 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
     // ---- publish (acc, m, l) of rows g < group (double-buffered scratch), hand off ----
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
-    const int sbuf = n_done & 1;
-    if (!wait_or_abort(a, sm, &sm.scr_empty[sbuf], ((uint32_t)(n_done >> 1) & 1u) ^ 1u)) return;
-    float* my_scr = sm.scratch + sbuf * sm.scratch_floats + (size_t)cw * G * (D + 2);
+    const int sbuf = n_done % a.nscr;
+    if (!wait_or_abort(a, sm, &sm.scr_empty[sbuf], ((uint32_t)(n_done / a.nscr) & 1u) ^ 1u)) return;
+    float* my_scr = sm.scratch + sbuf * sm.scratch_floats + (size_t)cw * group * state_stride(D);
     if (g < group) {
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
-        my_scr[g * (D + 2) + n * 8 + 2 * tq] = o[n][0];
-        my_scr[g * (D + 2) + n * 8 + 2 * tq + 1] = o[n][1];
+        my_scr[g * state_stride(D) + n * 8 + 2 * tq] = o[n][0];
+        my_scr[g * state_stride(D) + n * 8 + 2 * tq + 1] = o[n][1];
       }
       if (tq == 0) {
-        my_scr[g * (D + 2) + D] = m;
-        my_scr[g * (D + 2) + D + 1] = l;
+        my_scr[g * state_stride(D) + D] = m;
+        my_scr[g * state_stride(D) + D + 1] = l;
       }
     }
     hand_off<D, G, NCW>(a, sm, us, sbuf, uk, lane);
@@ -241,10 +252,95 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
       uphase ^= 1;
     }
   }
+  if constexpr (kTrace) {
+    if (a.trace && lane == 0 && blockIdx.x < kTraceMaxCta)
+      atomicMax(a.trace + kTraceCta + 4 * blockIdx.x + 3, gtime());
+  }
 }
 
-constexpr int kMmaNCW = 4;
-constexpr int kMmaRingTarget = 64 * 1024;  // leaves room for 2 CTAs per SM
+// Two configurations, both at 2 CTAs per SM.  Groups of up to 4 query heads:
+// 3 consumer warps, a 6-stage ring (96 KB of K/V in flight per CTA) and one
+// merge scratch buffer.  Larger groups need twice the scratch and take 4
+// consumer warps over a 4-stage ring (64 KB) with two scratch buffers.
+template <typename T, int D, int NCW>
+static int run_mma_cfg(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream, int ring_target, int nscr) {
+  auto kern = paged_decode_mma_kernel<T, D, NCW>;
+  const int bs = pool.block_size;
+  // Stages of >= 32 tokens: fixed per-stage costs (barrier round trips, copy
+  // issue) halve against 16-token stages.
+  const int sb = bs >= 32 ? 1 : 32 / bs;  // stages hold a multiple of 32 tokens
+  a.stage_blocks = sb;
+  a.nscr = nscr;
+  // launch configuration, worked out once per (device, block size, group)
+  struct Cfg {
+    int ok = 0, nstage = 0, ncw = 0, smem = 0, ctas = 0;
+  };
+  static std::mutex mu;
+  static std::unordered_map<long long, Cfg> cache;
+  static int attr_smem = 0;
+  Cfg c;
+  {
+    const long long key = ((long long)pool.device << 32) | ((long long)bs << 8) | a.group;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      c = it->second;
+    } else {
+      const int scratch = NCW * a.group * state_stride(D) * 4;
+      const int qb = a.group * D * (int)sizeof(T);
+      SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb, nscr);
+      int ncw = NCW;
+      int nstage = (ring_target / sp.stage_bytes) / ncw * ncw;
+      if (nstage < ncw) nstage = ncw;
+      sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb, nscr);
+      while (sp.total + 1024 > 200 * 1024 && nstage > 1) {
+        if (nstage > ncw) {
+          nstage -= ncw;
+        } else {
+          ncw = --nstage;
+        }
+        sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb, nscr);
+      }
+      const int smem = sp.total + 1024;  // 1024-byte alignment slack for the swizzled ring
+      if (smem > 227 * 1024) {
+        set_last_error("paged_decode: block_size %d x head_dim %d tile does not fit shared memory", bs, D);
+        return CLOVE_ERR_UNSUPPORTED;
+      }
+      // (the attribute belongs to the kernel: only raise it, so configurations
+      // cached for other block sizes stay launchable)
+      if (smem > attr_smem) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+          set_last_error("cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError()));
+          return CLOVE_ERR_CUDA;
+        }
+        attr_smem = smem;
+      }
+      int occ = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, (NCW + 1) * 32, smem) != cudaSuccess ||
+          occ < 1) {
+        cudaGetLastError();
+        occ = 1;
+      }
+      c.ok = 1;
+      c.nstage = nstage;
+      c.ncw = ncw;
+      c.smem = smem;
+      c.ctas = pool.num_sms * std::min(occ, kMaxCtasPerSm);
+      cache[key] = c;
+    }
+  }
+  a.nstage = c.nstage;
+  a.ncw = c.ncw;
+  a.num_ctas = c.ctas;
+  cudaError_t e = launch_dependent(kern, (unsigned)c.ctas, (NCW + 1) * 32, c.smem, stream, pool.tm_k_sw,
+                                   pool.tm_v_sw, a);
+  if (e != cudaSuccess) {
+    set_last_error("paged_decode (mma) launch: %s", cudaGetErrorString(e));
+    return CLOVE_ERR_CUDA;
+  }
+  count_launches(1);
+  return CLOVE_OK;
+}
 
 template <typename T, int D>
 int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
@@ -252,54 +348,8 @@ int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
     set_last_error("paged_decode: tensor-core kernel needs a 16-bit pool, block_size >= 8, group <= 8");
     return CLOVE_ERR_UNSUPPORTED;
   }
-  auto kern = paged_decode_mma_kernel<T, D, kMmaNCW>;
-  const int bs = pool.block_size;
-  // Stages of >= 32 tokens: fixed per-stage costs (barrier round trips, copy
-  // issue) halve against 16-token stages.
-  const int sb = bs >= 32 ? 1 : 32 / bs;  // stages hold a multiple of 32 tokens
-  a.stage_blocks = sb;
-  const int scratch = kMmaNCW * 8 * (D + 2) * 4;
-  const int qb = 8 * D * (int)sizeof(T);
-  SmemPlan sp = smem_plan(bs, D, sizeof(T), sb, 1, scratch, qb);
-  int ncw = kMmaNCW;
-  int nstage = (kMmaRingTarget / sp.stage_bytes) / ncw * ncw;
-  if (nstage < ncw) nstage = ncw;
-  if (nstage > 4 * ncw) nstage = 4 * ncw;
-  sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);
-  while (sp.total + 1024 > 200 * 1024 && nstage > 1) {
-    if (nstage > ncw) {
-      nstage -= ncw;
-    } else {
-      ncw = --nstage;
-    }
-    sp = smem_plan(bs, D, sizeof(T), sb, nstage, scratch, qb);
-  }
-  const int smem = sp.total + 1024;  // 1024-byte alignment slack for the swizzled ring
-  if (smem > 227 * 1024) {
-    set_last_error("paged_decode: block_size %d x head_dim %d tile does not fit shared memory", bs, D);
-    return CLOVE_ERR_UNSUPPORTED;
-  }
-  a.nstage = nstage;
-  a.ncw = ncw;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) {
-    set_last_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    return CLOVE_ERR_CUDA;
-  }
-  int occ = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, (kMmaNCW + 1) * 32, smem);
-  if (e != cudaSuccess || occ < 1) occ = 1;
-  long long units_max = (long long)a.batch * a.max_chunks * a.num_kv_heads;
-  long long grid = (long long)pool.num_sms * occ;
-  if (grid > units_max) grid = units_max;
-  if (grid < 1) grid = 1;
-  e = launch_dependent(kern, (unsigned)grid, (kMmaNCW + 1) * 32, smem, stream, pool.tm_k_sw, pool.tm_v_sw, a);
-  if (e != cudaSuccess) {
-    set_last_error("paged_decode (mma) launch: %s", cudaGetErrorString(e));
-    return CLOVE_ERR_CUDA;
-  }
-  count_launches(1);
-  return CLOVE_OK;
+  if (a.group <= 4) return run_mma_cfg<T, D, 3>(pool, a, stream, 96 * 1024, 1);
+  return run_mma_cfg<T, D, 4>(pool, a, stream, 64 * 1024, 2);
 }
 
 template int run_mma<__nv_bfloat16, 64>(const clove_pool&, DecodeArgs&, cudaStream_t);

@@ -12,27 +12,29 @@
 // kernels or symbols there) and stays until the process exits.
 //
 // Limits and rules:
-//   - The scratch is kNoAllocScratchBytes (32 MiB) per GPU; calls whose
+//   - The scratch is kNoAllocScratchBytes (16 MiB) per GPU; calls whose
 //     workspace need (clove_cuda_decode_workspace_size) exceeds it are
 //     rejected with CLOVE_ERR_WORKSPACE.
 //   - Every call on a GPU shares the one array and it keeps what the last
-//     call left there; the plan kernel of each call re-initialises everything
-//     the decode reads from it (item list, claim counter, check flags).  Calls
-//     that overlap on the GPU (other streams, other host threads) race on it:
-//     serialise them.
+//     call left there.  Each call writes every per-CTA descriptor and partial
+//     state it later reads, and its combine kernel leaves the flag word
+//     cleared for the next call, so leftovers of an earlier (larger or
+//     smaller) call are never read.  The array starts zeroed (static device
+//     memory).  Calls that overlap on the GPU (other streams, other host
+//     threads) race on it: serialise them.
 //   - The first call on a device looks up the array's device address (with
 //     that device current) and caches it; make that first call before any
 //     stream capture.  A failed lookup is not cached: the next call retries.
 //   - Device check flags (bad block ids, context lengths, a bounded wait that
-//     ran out) land in the array's first word, like the workspace call's;
-//     clove_cuda_noalloc_status reads and clears them.
+//     ran out) land in the array, as they land in a caller's workspace;
+//     clove_cuda_noalloc_status reads and clears those of the last call.
 #include <mutex>
 
 #include "host.h"
 
 namespace clove {
 
-constexpr size_t kNoAllocScratchBytes = 32u << 20;
+constexpr size_t kNoAllocScratchBytes = 16u << 20;
 constexpr int kMaxDevices = 64;
 
 // The scratch.  In host code this name is only a stand-in for the symbol,

@@ -14,10 +14,12 @@
 // Semantics follow the reference's FlashAttention step (src/lazy.rs:4821-4923:
 // causal mask, RoPE on q and k, scale 1/sqrt(head_dim)) with the exact
 // exponential in place of its polynomial approximation (lazy.rs:4846-4851).
+#include <algorithm>
 #include <cmath>
 
 #include "../../include/clove_cuda.h"
 #include "common.cuh"
+
 #include "host.h"
 
 namespace clove {
@@ -122,7 +124,7 @@ static PrefillLayout prefill_layout(const clove_pool& pool, int num_tokens, int 
   L.off_lens = off;
   off = al256(off + (size_t)num_tokens * 4);
   L.off_decode = off;
-  off += decode_layout(pool, num_tokens, num_q_heads, max_ctx).total;
+  off += std::max(decode_layout(pool, num_tokens, num_q_heads, max_ctx).total, prefill_mma_scratch_bytes(num_tokens));
   L.total = off;
   return L;
 }

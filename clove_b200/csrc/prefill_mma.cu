@@ -481,9 +481,11 @@ static int run_prefill(const clove_pool& pool, PrefillArgs& a, cudaStream_t stre
   return CLOVE_OK;
 }
 
+size_t prefill_mma_scratch_bytes(int num_tokens) { return 512 + sizeof(int2) * (size_t)num_tokens; }
+
 // Tensor-core prefill of already rotated queries (q_rot) over a cache that
 // already holds the prompt's K/V.  ws: scratch of at least
-// decode_layout(pool, num_tokens, ...) bytes.  Returns CLOVE_ERR_UNSUPPORTED
+// prefill_mma_scratch_bytes(num_tokens) bytes.  Returns CLOVE_ERR_UNSUPPORTED
 // (nothing launched) when the shape is not covered.
 int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                        const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
@@ -492,7 +494,6 @@ int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, co
   if (pool.elem_bytes != 2 || !pool.has_swizzled || pool.block_size < 8 || group > 16 ||
       (pool.head_dim != 64 && pool.head_dim != 128))
     return CLOVE_ERR_UNSUPPORTED;
-  const DecodeLayout L = decode_layout(pool, num_tokens, num_q_heads, max_ctx);
   unsigned char* w = static_cast<unsigned char*>(ws);
   PrefillArgs a;
   a.q = q_rot;
@@ -500,10 +501,10 @@ int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, co
   a.cu_seqlens = cu_seqlens;
   a.context_lens = context_lens;
   a.block_tables = block_tables;
-  a.items = reinterpret_cast<int2*>(w + L.off_items);  // room for num_tokens * max_chunks >= tiles
-  a.n_items = reinterpret_cast<int32_t*>(w + L.off_nitems);
-  a.unit_counter = reinterpret_cast<int32_t*>(w + L.off_nitems) + 2;
-  a.err = reinterpret_cast<int32_t*>(w + L.off_err);
+  a.items = reinterpret_cast<int2*>(w + 512);  // tiles <= num_tokens
+  a.n_items = reinterpret_cast<int32_t*>(w + 256);
+  a.unit_counter = reinterpret_cast<int32_t*>(w + 256) + 2;
+  a.err = reinterpret_cast<int32_t*>(w);
   a.bt_stride = bt_stride;
   a.batch = batch;
   a.hq = num_q_heads;

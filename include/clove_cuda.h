@@ -130,8 +130,10 @@ int clove_cuda_gather_kv(clove_pool_t pool, const int32_t* block_tables,
                          void* stream);
 
 /* Bytes of scratch workspace paged_decode / paged_append_decode need for
- * this batch, head count and maximum context length (tokens attended,
- * i.e. including the appended token). */
+ * this head count (the batch and context-length arguments are kept for the
+ * interface: the decode splits its work evenly over a fixed number of CTAs,
+ * each keeping at most two partial states, so the scratch does not grow with
+ * them; a few MB). */
 size_t clove_cuda_decode_workspace_size(clove_pool_t pool, int batch,
                                         int num_q_heads, int max_ctx);
 
@@ -140,8 +142,9 @@ size_t clove_cuda_decode_workspace_size(clove_pool_t pool, int batch,
  * over the context_lens[b] cached tokens of sequence b (semantics of
  * src/nn/attention.rs:52-69; gather of src/lazy.rs:5259-5270).  A sequence
  * with context length 0 gets a zero output row.  `workspace` (device memory,
- * >= clove_cuda_decode_workspace_size bytes, 256-byte aligned) is scratch;
- * the call allocates nothing. */
+ * >= clove_cuda_decode_workspace_size bytes, 256-byte aligned) is scratch:
+ * ZERO-FILLED before its first use (its check-flag words), after which calls
+ * on one stream keep sharing it; the call allocates nothing. */
 int clove_cuda_paged_decode(clove_pool_t pool, const void* q, int num_q_heads,
                             const int32_t* block_tables, int bt_stride,
                             const int32_t* context_lens, int batch,
@@ -238,7 +241,7 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x,
  * whose device memory comes only from an allocator it may not call on the
  * serving path).  No counterpart in the reference.  Same arguments and
  * results as clove_cuda_paged_append_decode, minus the workspace: scratch
- * comes from a fixed 32 MiB array in the library's device code, placed on a
+ * comes from a fixed 16 MiB array in the library's device code, placed on a
  * GPU when the library's device code is first loaded there and kept until
  * the process exits.  Returns CLOVE_ERR_WORKSPACE when the call needs more
  * than that (see clove_cuda_decode_workspace_size).  All calls on a GPU
@@ -264,9 +267,10 @@ int clove_cuda_paged_append_decode_noalloc(clove_pool_t pool, const void* q,
 int clove_cuda_noalloc_status(int device, void* stream, int* flags);
 
 /* Synchronise `stream` and read the device check flags (CLOVE_FLAG_*) that
- * the most recent decode call on `workspace` raised (each call clears them
- * when it starts); the word is cleared after reading.  Returns
- * CLOVE_ERR_DEVICE_CHECK if any flag was set, CLOVE_OK otherwise. */
+ * the most recent completed decode call on `workspace` raised (each call
+ * publishes its own flags when it completes); the word is cleared after
+ * reading.  Returns CLOVE_ERR_DEVICE_CHECK if any flag was set, CLOVE_OK
+ * otherwise. */
 int clove_cuda_decode_status(void* workspace, void* stream, int* flags);
 
 /* Kernel-variant selection for decode: 0 = automatic (default), 1 = force
@@ -280,10 +284,12 @@ uint64_t clove_cuda_launch_count(void);
 
 /* Testing hook (failure detection without a GPU fault).  wait_limit: polls
  * after which a pipeline wait gives up (0 = the default, seconds of wall
- * time); inject_stall = 1 makes one CTA's producer skip one stage's copy, so
- * its consumer's bounded wait runs out: the call then completes, reports
- * CLOVE_FLAG_TIMEOUT through clove_cuda_decode_status, and its output is
- * undefined.  Process-wide; never set it in production. */
+ * time); inject_stall = 1 makes producers skip one stage's copy (decode:
+ * the first stage of every CTA's first piece; fused projection: the first
+ * stage of the first CTA), so the consumers' bounded waits run out: the call
+ * then completes, reports CLOVE_FLAG_TIMEOUT through clove_cuda_decode_status
+ * (the pool's status for the projection), and its output is undefined.
+ * Process-wide; never set it in production. */
 int clove_cuda_debug_set(uint32_t wait_limit, int inject_stall);
 
 /* Measurement hook: with enable = 1, every decode call records CUDA events
@@ -295,6 +301,13 @@ int clove_cuda_debug_set(uint32_t wait_limit, int inject_stall);
 int clove_cuda_debug_phase_timing(int enable);
 int clove_cuda_debug_phase_ms(float* plan_ms, float* decode_ms,
                               float* combine_ms);
+
+/* Measurement hook of timeline builds (compiled with -DCLOVE_TRACE): decode
+ * calls write %globaltimer stamps of the plan, every CTA and every work unit
+ * into `buffer` (device memory, at least (16 + 4*4096 + 3*65536) u64, plan
+ * and combine slots 0..3 preset by the caller); NULL stops it.  Returns
+ * CLOVE_ERR_UNSUPPORTED in the product build, which records nothing. */
+int clove_cuda_debug_trace(void* buffer);
 
 #ifdef __cplusplus
 }
