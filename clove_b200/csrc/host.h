@@ -98,6 +98,10 @@ cudaError_t launch_dependent(Kern kern, unsigned grid, unsigned threads, size_t 
 }
 
 size_t prefill_mma_scratch_bytes(int num_tokens);
+bool prefill_tc_supported(const clove_pool& pool, int num_q_heads);
+int launch_prefill_tc(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
+                      const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
+                      int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);
 int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                        const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
                        int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);

@@ -15,6 +15,7 @@
 // causal mask, RoPE on q and k, scale 1/sqrt(head_dim)) with the exact
 // exponential in place of its polynomial approximation (lazy.rs:4846-4851).
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 
 #include "../../include/clove_cuda.h"
@@ -213,8 +214,20 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, co
     int prev2 = -1;
     cudaGetDevice(&prev2);
     if (prev2 != pool->device) cudaSetDevice(pool->device);
-    const int rc = launch_prefill_mma(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride,
-                                      batch, num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);
+    int rc = CLOVE_ERR_UNSUPPORTED;
+    // 5th-generation tensor cores where the shape is covered (16-bit pools,
+    // head_dim 128, group dividing 128, block_size dividing 128), unless the
+    // warp-MMA variant is forced (2)
+    static const bool tc_on = [] {
+      const char* v = std::getenv("CLOVE_PREFILL_TC");
+      return v && v[0] == '1';
+    }();
+    if (tc_on && decode_variant() == 0 && prefill_tc_supported(*pool, num_q_heads))
+      rc = launch_prefill_tc(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride, batch,
+                             num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);
+    if (rc == CLOVE_ERR_UNSUPPORTED)
+      rc = launch_prefill_mma(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride, batch,
+                              num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);
     if (prev2 >= 0 && prev2 != pool->device) cudaSetDevice(prev2);
     if (rc != CLOVE_ERR_UNSUPPORTED) return rc;
   }

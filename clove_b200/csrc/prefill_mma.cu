@@ -20,27 +20,12 @@
 #include "decode_common.cuh"
 #include "host.h"
 #include "mma_common.cuh"
+#include "prefill_common.cuh"
 
 namespace clove {
 
 constexpr int kPfNCW = 4;      // consumer warps, 16 query rows each
 constexpr int kPfRows = 64;    // query rows per unit
-constexpr int kPfBins = 256;   // size bins of the longest-first ordering
-
-struct PrefillArgs {
-  const void* q;                // rotated queries [T, Hq, D]
-  float* out;                   // [T, Hq, D]
-  const int32_t* cu_seqlens;    // [B + 1]
-  const int32_t* context_lens;  // [B]
-  const int32_t* block_tables;  // [B, bt_stride]
-  int2* items;                  // (b, tile)
-  int32_t* n_items;
-  int32_t* unit_counter;
-  int32_t* err;
-  int bt_stride, batch, hq, hkv, group, bs, num_blocks, tq, nstage, sb, max_ctx;
-  uint32_t wait_limit;
-  float qscale;                 // scale * log2(e)
-};
 
 // Work list: every (sequence, token tile), ordered by key count (context +
 // tile end) descending through a counting sort over kPfBins bins.

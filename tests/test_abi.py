@@ -124,3 +124,11 @@ def test_workload_layouts_disjoint():
     c2 = make_layout(CONFIGS["c2"])
     assert c2.block_tables.shape == (64, 129) and (c2.context_lens == 2048).all()
     assert c2.kv_bytes() == 64 * 2049 * 2 * 32 * 128 * 4
+
+
+def test_rust_binding_declares_every_entry_point():
+    # rust/src/cuda_ffi.rs (the crate's extern "C" block) names exactly the
+    # functions include/clove_cuda.h declares
+    from clove_b200 import _lib
+    text = (ROOT / "rust" / "src" / "cuda_ffi.rs").read_text()
+    assert set(re.findall(r"pub fn (clove_\w+)", text)) == set(_lib.SIGNATURES)

@@ -113,3 +113,85 @@ def test_prefill_long_prompt_multi_chunk():
                             (rows + 1).astype(np.int32), 1.0 / np.sqrt(128))
     ok, worst = oracle.tolerance_ok(out.cpu().numpy()[rows], ref, 2e-2)
     assert ok, worst
+
+
+def _prefill_vs_oracle(dtype, hq, hkv, d, bs, theta, prior, prompt, seed, variant="auto"):
+    import oracle
+    from clove_b200 import KVPool, set_decode_variant
+    c = _case(dtype, hq, hkv, d, bs, prior=prior, prompt=prompt, seed=seed)
+    pool = KVPool(c["nb"], bs, hkv, d, dtype, 0)
+    pool.storage.normal_()
+    before = to_numpy_bits(pool.storage)
+    dev = torch.device("cuda", 0)
+    set_decode_variant(variant)
+    try:
+        out = pool.prefill(c["q"], c["k"], c["v"], torch.from_numpy(c["cu"]).to(dev),
+                           torch.from_numpy(c["bt"]).to(dev), torch.from_numpy(c["ctx"]).to(dev),
+                           max_ctx=int(c["total"].max()), rope_theta=theta)
+        torch.cuda.synchronize()
+    finally:
+        set_decode_variant("auto")
+    assert pool.pool_status() == 0
+    kn, vn, qn = (to_numpy_bits(t) for t in (c["k"], c["v"], c["q"]))
+    pos = np.concatenate([c["ctx"][b] + np.arange(c["cu"][b + 1] - c["cu"][b]) for b in range(c["B"])])
+    seq = np.concatenate([[b] * (c["cu"][b + 1] - c["cu"][b]) for b in range(c["B"])])
+    slots = np.array([c["bt"][s, p // bs] * bs + p % bs for s, p in zip(seq, pos)])
+    kc = _bits_to_f64(before[0], dtype).reshape(-1, hkv, d)
+    vc = _bits_to_f64(before[1], dtype).reshape(-1, hkv, d)
+    kf, qf = _bits_to_f64(kn, dtype), _bits_to_f64(qn, dtype)
+    if theta > 0:
+        kf, qf = oracle.rope(kf, pos, theta), oracle.rope(qf, pos, theta)
+    kc[slots] = kf
+    vc[slots] = _bits_to_f64(vn, dtype)
+    ref = oracle.decode_f64(0, np.ascontiguousarray(qf.astype(np.float32)),
+                            kc.reshape(c["nb"], bs, hkv, d).astype(np.float32),
+                            vc.reshape(c["nb"], bs, hkv, d).astype(np.float32), c["bt"][seq], pos + 1, 1.0 / np.sqrt(d))
+    from workload_check import tol_check
+    tol_check(out.cpu().numpy(), ref, 2e-2)
+    return out
+
+
+@pytest.mark.parametrize("dtype,hq,hkv,bs,theta", [
+    (torch.bfloat16, 8, 2, 32, 10000.0),   # group 4
+    (torch.bfloat16, 16, 2, 16, 0.0),      # group 8
+    (torch.float16, 32, 2, 64, 500.0),     # group 16
+    (torch.bfloat16, 4, 4, 8, 10000.0),    # group 1
+    (torch.float16, 4, 2, 128, 0.0),       # group 2, one block per key step
+])
+def test_prefill_tensor_core_multi_step(dtype, hq, hkv, bs, theta):
+    # contexts and prompts spanning several 128-key steps, prompt tails
+    # shorter than a query tile, and a prompt continuing a cached context
+    _prefill_vs_oracle(dtype, hq, hkv, 128, bs, theta, prior=[300, 0, 129, 7], prompt=[200, 257, 1, 95], seed=hq + bs)
+
+
+def test_prefill_tensor_core_matches_warp_mma():
+    # the tcgen05 kernel and the warp-MMA kernel agree (both against the oracle)
+    a = _prefill_vs_oracle(torch.bfloat16, 16, 4, 128, 32, 10000.0, prior=[50, 0], prompt=[400, 130], seed=3)
+    b = _prefill_vs_oracle(torch.bfloat16, 16, 4, 128, 32, 10000.0, prior=[50, 0], prompt=[400, 130], seed=3,
+                           variant="mma")
+    assert torch.isfinite(a).all() and torch.isfinite(b).all()
+
+
+def test_prefill_tensor_core_stuck_wait_times_out():
+    # failure detection without a GPU fault: one K/V step is never filled, the
+    # bounded waits run out, the call completes with CLOVE_FLAG_TIMEOUT in the
+    # pool's status word, and the next call on the same context is correct
+    import time
+
+    from clove_b200 import KVPool, _lib
+    L = _lib.lib()
+    c = _case(torch.bfloat16, 8, 2, 128, 32, prior=[0, 100], prompt=[300, 60], seed=5)
+    pool = KVPool(c["nb"], 32, 2, 128, torch.bfloat16, 0)
+    dev = torch.device("cuda", 0)
+    try:
+        _lib.check(L.clove_cuda_debug_set(2000, 1))
+        t0 = time.time()
+        pool.prefill(c["q"], c["k"], c["v"], torch.from_numpy(c["cu"]).to(dev), torch.from_numpy(c["bt"]).to(dev),
+                     torch.from_numpy(c["ctx"]).to(dev), max_ctx=int(c["total"].max()))
+        flags = pool.pool_status()
+        elapsed = time.time() - t0
+    finally:
+        L.clove_cuda_debug_set(0, 0)
+    assert flags & _lib.FLAG_TIMEOUT, flags
+    assert elapsed < 30
+    _prefill_vs_oracle(torch.bfloat16, 8, 2, 128, 32, 0.0, prior=[0, 100], prompt=[300, 60], seed=5)
