@@ -207,9 +207,10 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, co
     return CLOVE_ERR_CUDA;
   }
   count_launches(1);
-  // Tensor-core prefill kernel where the shape is covered (16-bit pools,
-  // head_dim 64/128, group <= 16), unless the CUDA-core variant is forced;
-  // otherwise every prompt token runs as a decode query row over the cache.
+  // Tensor-core prefill where the shape is covered: tcgen05 (prefill_tc.cu)
+  // first, then the warp-MMA kernel (16-bit pools, head_dim 64/128, group
+  // <= 16), unless the CUDA-core variant is forced; otherwise every prompt
+  // token runs as a decode query row over the cache.
   if (decode_variant() != 1) {
     int prev2 = -1;
     cudaGetDevice(&prev2);
@@ -218,11 +219,7 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, co
     // 5th-generation tensor cores where the shape is covered (16-bit pools,
     // head_dim 128, group dividing 128, block_size dividing 128), unless the
     // warp-MMA variant is forced (2)
-    static const bool tc_on = [] {
-      const char* v = std::getenv("CLOVE_PREFILL_TC");
-      return v && v[0] == '1';
-    }();
-    if (tc_on && decode_variant() == 0 && prefill_tc_supported(*pool, num_q_heads))
+    if (decode_variant() == 0 && prefill_tc_supported(*pool, num_q_heads))
       rc = launch_prefill_tc(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride, batch,
                              num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);
     if (rc == CLOVE_ERR_UNSUPPORTED)

@@ -17,10 +17,11 @@
 //               operands K-major in shared memory (128-byte swizzle), the f32
 //               result in one of two 128-column tensor-memory buffers;
 //   softmax     one thread per row reads its 128 scores from tensor memory,
-//               applies the causal mask and scale, updates the running max and
-//               sum, and writes P (16-bit) to shared memory as a K-major
-//               operand; when its max rose it rescales its O row in tensor
-//               memory (after the previous P.V finished);
+//               applies the causal mask and scale, updates its reference
+//               max and sum, and writes P (16-bit) to shared memory as a
+//               K-major operand; only when its max rose by more than 2^8 does
+//               it move the reference and rescale its O row in tensor memory
+//               (after the previous P.V finished);
 //   O += P V    tcgen05.mma, M 128 x N 128 dims x K 128 keys, P K-major and V
 //               MN-major (the cache rows are dim-contiguous), O in tensor
 //               memory for the whole unit.
@@ -89,6 +90,14 @@ __device__ __forceinline__ void tmem_ld_row128(uint32_t taddr, float (&v)[128]) 
     for (int k = 0; k < 16; ++k) v[16 * i + k] = __uint_as_float(r[i][k]);
 }
 
+// 2^x with the tensor-core path's accuracy needs (P is rounded to 16 bits
+// next): the special-function unit's approximation, -inf -> +0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 template <typename T>
@@ -108,8 +117,11 @@ template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
-  __shared__ __align__(8) uint64_t q_full, q_empty, pv_done, o_empty, drain;
+  __shared__ __align__(8) uint64_t q_full, q_empty, o_empty, drain;
   __shared__ __align__(8) uint64_t kv_full[kStages], kv_empty[kStages], s_full[2], s_empty[2], p_full[2];
+  // P.V of P index i completes phase i / 2 of pv_done[i % 2]: a waiter is never more than one phase
+  // behind (the next completion on that barrier needs a P the waiter has not produced yet)
+  __shared__ __align__(8) uint64_t pv_done[2];
   __shared__ __align__(8) uint64_t ufull[2], uempty[2];
   __shared__ TcUnit slots[2];
   __shared__ uint32_t tmem_slot;
@@ -127,7 +139,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
     mbar_init(&q_empty, 1);
-    mbar_init(&pv_done, 1);
     mbar_init(&o_empty, kTcRows);
     mbar_init(&drain, 1);
     for (int i = 0; i < kStages; ++i) {
@@ -138,6 +149,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], kTcRows);
       mbar_init(&p_full[i], kTcRows);
+      mbar_init(&pv_done[i], 1);
       mbar_init(&ufull[i], 1);
       mbar_init(&uempty[i], 1 + kTcRows / 32);  // the MMA thread + one arrival per softmax warp
     }
@@ -185,7 +197,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ------------------------------------------------------------ producer
     const uint64_t pol = policy_evict_first();
     const int bs = a.bs, bps = kTcKeys / bs;  // blocks per step
-    int ui = 0, g = 0;
+    int ui = 0, g = 0, stalled_g = -1;
     bool ok = true;
     while (ok) {
       int u = 0;
@@ -233,6 +245,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int s = 0; s < x.nsteps && ok; ++s, ++g) {
         const int nxt = s + 1 < x.nsteps ? table(s + 1) : 0;
         const int st = g % kStages;
+        if (a.inject_stall && u == 0 && s == 0) stalled_g = g;
         const int nb = min(bps, nblk - s * bps);
         int phys[16];
 #pragma unroll
@@ -240,7 +253,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
           if (!wait(&kv_empty[st], ((uint32_t)(g / kStages) & 1u) ^ 1u)) {
             ok = false;
-          } else if (a.inject_stall && blockIdx.x == 0 && g == 0) {
+          } else if (a.inject_stall && u == 0 && s == 0) {
             // test hook: this step is never filled, so the MMA warp's wait runs out
           } else {
             mbar_arrive_expect_tx(&kv_full[st], (uint32_t)nb * (uint32_t)bs * 128u * 4u);
@@ -266,7 +279,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       // drain: copies in flight must land before the CTA exits
       for (int t = max(0, g - kStages); t < g; ++t) {
-        if (a.inject_stall && blockIdx.x == 0 && t == 0) continue;
+        if (a.inject_stall && t == stalled_g) continue;
         for (uint32_t i = 0; i < a.wait_limit; ++i)
           if (mbar_try_wait(&kv_full[t % kStages], (uint32_t)(t / kStages) & 1u)) break;
       }
@@ -329,7 +342,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                          sw128_mnmajor_desc(va + (uint32_t)(64 * c + 16 * k) * 128u, kHalfBytes, 1024), idesc_pv,
                          (t == 0 && c == 0 && k == 0) ? 0u : 1u);
             umma_commit(&kv_empty[st]);
-            umma_commit(&pv_done);
+            umma_commit(&pv_done[pb]);
             ++pc;
           }
         }
@@ -347,19 +360,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int r = (warp & 3) * 32 + lane;  // this thread's row = tensor-memory lane
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const int t_in = r / G, gq = r - (r / G) * G;
-    int ui = 0, g = 0, sc = 0, pc = 0, pvc = 0;
-    // wait until `n` P.V steps have completed (they complete in order)
-    auto pv_wait = [&](int n) -> bool {
-      while (pvc < n) {
-        if (!wait(&pv_done, (uint32_t)pvc & 1u)) return false;
-        ++pvc;
-      }
-      return true;
+    int ui = 0, g = 0, sc = 0, pc = 0;
+    // Waits here are warp-uniform: the tensor-memory loads and stores that
+    // follow are warp-collective (.sync.aligned), so no lane may leave early.
+    auto wait_w = [&](uint64_t* bar, uint32_t parity) -> bool {
+      const bool r = wait(bar, parity);
+      return __all_sync(0xffffffffu, r ? 1 : 0) != 0;
+    };
+    // wait until P.V of P index i has completed (i < 0: nothing to wait for)
+    auto pv_wait = [&](int i) -> bool {
+      return i < 0 || wait_w(&pv_done[i & 1], (uint32_t)(i >> 1) & 1u);
     };
     bool ok = true;
     while (ok) {
       const int uk = ui & 1;
-      if (!wait(&ufull[uk], (uint32_t)(ui >> 1) & 1u)) break;
+      if (!wait_w(&ufull[uk], (uint32_t)(ui >> 1) & 1u)) break;
       const TcUnit x = slots[uk];
       __syncwarp();
       if (lane == 0) mbar_arrive(&uempty[uk]);
@@ -372,7 +387,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       float m = -INFINITY, l = 0.f;
       for (int s = 0; s < x.nsteps && ok; ++s) {
         const int sb = sc & 1;
-        if (!wait(&s_full[sb], (uint32_t)(sc >> 1) & 1u)) {
+        if (!wait_w(&s_full[sb], (uint32_t)(sc >> 1) & 1u)) {
           ok = false;
           break;
         }
@@ -383,26 +398,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_arrive(&s_empty[sb]);
         ++sc;
         const int key0 = s * kTcKeys;
+        // row max of the raw scores (the scale is positive); the causal mask
+        // only on steps that reach past this row's position
         float mx = -INFINITY;
+        if (key0 + kTcKeys - 1 <= pos) {
 #pragma unroll
-        for (int k = 0; k < kTcKeys; ++k) {
-          v[k] = key0 + k <= pos ? v[k] * a.qscale : -INFINITY;
-          mx = fmaxf(mx, v[k]);
+          for (int k = 0; k < kTcKeys; ++k) mx = fmaxf(mx, v[k]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < kTcKeys; ++k) {
+            v[k] = key0 + k <= pos ? v[k] : -INFINITY;
+            mx = fmaxf(mx, v[k]);
+          }
         }
-        const float m_new = fmaxf(m, mx);
+        mx *= a.qscale;  // log2 domain
+        // P is taken relative to a reference m that moves only when the row's
+        // max rises by more than 8 (log2 units): P <= 2^8 stays exact enough
+        // in 16 bits and the sums in f32, and O is rescaled (a wait on the
+        // previous P.V) only on those rare jumps.
+        const bool move = mx > m + 8.f;  // also true on the first visible key (m = -inf)
+        const float m_new = move ? mx : m;
         const float ref = m_new == -INFINITY ? 0.f : m_new;
-        const float corr = exp2f(m - ref);
+        const float corr = move ? exp2f(m - ref) : 1.f;  // 0 when m was -inf
         float rs = 0.f;
 #pragma unroll
         for (int k = 0; k < kTcKeys; ++k) {
-          v[k] = exp2f(v[k] - ref);
+          v[k] = ex2_approx(fmaf(v[k], a.qscale, -ref));
           rs += v[k];
         }
         l = l * corr + rs;
-        const bool rescale = s > 0 && m != m_new && m != -INFINITY;
+        const bool rescale = move && s > 0 && m != -INFINITY;
         m = m_new;
-        // P buffer pc & 1 was last read by P.V step pc - 2
-        if (!pv_wait(pc - 1)) {
+        // P buffer pc & 1 was last read by the P.V of P index pc - 2
+        if (!pv_wait(pc - 2)) {
           ok = false;
           break;
         }
@@ -419,19 +447,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             *reinterpret_cast<uint4*>(prow + (size_t)c * (kPBytes / 2) + ((w ^ (r & 7)) << 4)) = q4;
           }
         }
-        if (rescale) {
-          // the previous P.V must have finished writing O
-          if (!pv_wait(pc)) {
+        if (__any_sync(0xffffffffu, rescale ? 1 : 0)) {
+          // the previous P.V must have finished writing O; the whole warp
+          // takes part (rows whose max did not rise scale by 1)
+          if (!pv_wait(pc - 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const float f = rescale ? corr : 1.f;
 #pragma unroll 1
           for (int i = 0; i < 8; ++i) {
             float t16[16];
             tmem_ld16(tmem + lane_off + kTmemO + 16 * i, t16);
 #pragma unroll
-            for (int k = 0; k < 16; ++k) t16[k] *= corr;
+            for (int k = 0; k < 16; ++k) t16[k] *= f;
             tmem_st16(tmem + lane_off + kTmemO + 16 * i, t16);
           }
         }
@@ -439,7 +469,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           // V rows past the last key may hold any bits (P is 0 there, but
           // 0 * NaN is NaN inside the MMA): zero them once the copies landed
           const int st = (g + s) % kStages;
-          if (!wait(&kv_full[st], (uint32_t)((g + s) / kStages) & 1u)) {
+          if (!wait_w(&kv_full[st], (uint32_t)((g + s) / kStages) & 1u)) {
             ok = false;
             break;
           }
@@ -459,7 +489,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (!ok) break;
       // ---- epilogue: O / l for valid rows ----
-      if (!pv_wait(pc)) break;
+      if (!pv_wait(pc - 1)) break;
       tc_fence_after();
       {
         const float inv = l > 0.f ? 1.f / l : 0.f;

@@ -136,13 +136,22 @@ def _prefill_vs_oracle(dtype, hq, hkv, d, bs, theta, prior, prompt, seed, varian
     pos = np.concatenate([c["ctx"][b] + np.arange(c["cu"][b + 1] - c["cu"][b]) for b in range(c["B"])])
     seq = np.concatenate([[b] * (c["cu"][b + 1] - c["cu"][b]) for b in range(c["B"])])
     slots = np.array([c["bt"][s, p // bs] * bs + p % bs for s, p in zip(seq, pos)])
-    kc = _bits_to_f64(before[0], dtype).reshape(-1, hkv, d)
-    vc = _bits_to_f64(before[1], dtype).reshape(-1, hkv, d)
+    # the kernels store the rotated rows in the pool dtype: attend over the
+    # cache as written (its prompt rows checked against the rotation below)
+    # with q rotated and rounded the same way
+    after = to_numpy_bits(pool.storage)
+    kc = _bits_to_f64(after[0], dtype).reshape(-1, hkv, d)
+    vc = _bits_to_f64(after[1], dtype).reshape(-1, hkv, d)
     kf, qf = _bits_to_f64(kn, dtype), _bits_to_f64(qn, dtype)
     if theta > 0:
         kf, qf = oracle.rope(kf, pos, theta), oracle.rope(qf, pos, theta)
-    kc[slots] = kf
-    vc[slots] = _bits_to_f64(vn, dtype)
+    qf = torch.from_numpy(qf).to(dtype).double().numpy()
+    assert np.abs(kc[slots] - kf).max() <= 2.0 ** -7 * np.abs(kf).max()  # one 16-bit rounding of the rotation
+    assert np.array_equal(vc[slots], _bits_to_f64(vn, dtype))
+    unchanged = np.ones(kc.shape[0], bool)
+    unchanged[slots] = False
+    assert np.array_equal(after[0].reshape(-1, hkv, d)[unchanged].view(np.uint8),
+                          before[0].reshape(-1, hkv, d)[unchanged].view(np.uint8))
     ref = oracle.decode_f64(0, np.ascontiguousarray(qf.astype(np.float32)),
                             kc.reshape(c["nb"], bs, hkv, d).astype(np.float32),
                             vc.reshape(c["nb"], bs, hkv, d).astype(np.float32), c["bt"][seq], pos + 1, 1.0 / np.sqrt(d))
