@@ -246,89 +246,99 @@ __global__ void __launch_bounds__((NCW + 1) * 32)
 constexpr int kCombineThreads = 128;
 constexpr int kCombineMaxPieces = 1024;  // >= P (decode CTAs) - checked on the host
 
-// States staged in shared memory per round (8 rows of head_dim + 4 floats
-// each; fewer for head_dim 256 to stay within static shared memory); more
-// pieces are merged in rounds, the running state taking one entry of the
-// next round.
-template <int D>
-__host__ __device__ constexpr int combine_stage() { return D > 128 ? 4 : 8; }
-constexpr int kWtsL = 64, kWtsM = 72;  // wts[]: row sums and maxima after the per-state weights
+// Pieces merged per pass (more are merged in passes, carrying a running state).
+constexpr int kCombinePass = 256;
 
 // Merge the np partial states listed in pieces[] (partial slot indices
-// c * 2 + slot) of segment (b, h) and write its output rows.  All threads of
-// the CTA take part.  Each round stages up to kCombineStage states in shared
-// memory with one batch of independent 16-byte loads, then per row g:
-// M = max_i m_i, w_i = 2^(m_i - M), L = sum_i w_i l_i, acc = sum_i w_i acc_i.
+// c * 2 + slot) of segment (b, h) and write outputs [o_begin, o_end) of its
+// rows (output o = row o / (D/4), dims 4 (o % (D/4)) ..).  All threads of the
+// CTA take part; per pass, every load of a phase is independent of the
+// others, so a pass costs a few memory round trips whatever the piece count:
+//   1. (m, l) of every (piece, row) into shared memory;
+//   2. per row g: M = max_i m_i, w_i = 2^(m_i - M), L = sum_i w_i l_i;
+//   3. each thread sums four dims of one row over all pieces (16-byte loads).
 template <int D>
-__device__ void combine_segment(const DecodeArgs& a, int b, int h, const int* pieces, int np, float* st,
-                                float* wts, float* run) {
+__device__ void combine_segment(const DecodeArgs& a, int b, int h, const int* pieces, int np, float* pm, float* pl,
+                                float* run, float* rowv, int o_begin, int o_end) {
   constexpr int S = state_stride(D);
+  constexpr int NW = kCombineThreads / 32;
   const int group = a.group;
   const int Hq = a.num_kv_heads * group;
-  const int tid = threadIdx.x;
-  const int row4 = S / 4;  // float4 per state row
-  bool have_run = false;
-  for (int base = 0; base < np;) {
-    const int first = have_run ? 1 : 0;
-    const int n = min(combine_stage<D>() - first, np - base);
-    const int ne = n + first;
-    if (have_run)
-      for (int i = tid; i < group * row4; i += kCombineThreads)
-        reinterpret_cast<float4*>(st)[i] = reinterpret_cast<const float4*>(run)[i];
-    for (int i = tid; i < n * group * row4; i += kCombineThreads) {
-      const int p = i / (group * row4), r = i - p * (group * row4);
-      reinterpret_cast<float4*>(st)[first * group * row4 + i] =
-          __ldcg(reinterpret_cast<const float4*>(a.partials + (size_t)pieces[base + p] * group * S) + r);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* rowM = rowv;         // [8] reference max of the pass
+  float* rowL = rowv + 8;     // [8] sum of weights times l (running)
+  float* rowR = rowv + 16;    // [8] factor on the running state
+  for (int base = 0; base < np; base += kCombinePass) {
+    const int n = min(kCombinePass, np - base);
+    const bool first = base == 0, last = base + n >= np;
+    for (int i = tid; i < n * group; i += kCombineThreads) {
+      const int p = i / group, g = i - p * group;
+      const float* src = a.partials + ((size_t)pieces[base + p] * group + g) * S;
+      pm[i] = __ldcg(src + D);
+      pl[i] = __ldcg(src + D + 1);
     }
     __syncthreads();
-    for (int g = tid >> 5; g < group; g += kCombineThreads / 32) {
-      const int lane = tid & 31;
-      float M = -INFINITY;
-      for (int i = lane; i < ne; i += 32) M = fmaxf(M, st[(i * group + g) * S + D]);
+    for (int g = warp; g < group; g += NW) {
+      float M = first ? -INFINITY : rowM[g];
+      for (int i = lane; i < n; i += 32) M = fmaxf(M, pm[i * group + g]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
       float ls = 0.f;
-      for (int i = lane; i < ne; i += 32) {
-        const float mi = st[(i * group + g) * S + D];
+      for (int i = lane; i < n; i += 32) {
+        const float mi = pm[i * group + g];
         const float wi = mi == -INFINITY ? 0.f : exp2f(mi - M);
-        wts[i * group + g] = wi;
-        ls = fmaf(wi, st[(i * group + g) * S + D + 1], ls);
+        pm[i * group + g] = wi;  // the weight replaces m
+        ls = fmaf(wi, pl[i * group + g], ls);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
       if (lane == 0) {
-        wts[kWtsL + g] = ls;
-        wts[kWtsM + g] = M;
+        const float r = first || rowM[g] == -INFINITY ? 0.f : exp2f(rowM[g] - M);
+        rowR[g] = r;
+        rowL[g] = (first ? 0.f : rowL[g] * r) + ls;
+        rowM[g] = M;
       }
     }
     __syncthreads();
-    base += n;
-    const bool last_round = base >= np;
-    for (int idx = tid; idx < group * D; idx += kCombineThreads) {
-      const int g = idx / D, d = idx - (idx / D) * D;
-      float o = 0.f;
-      for (int i = 0; i < ne; ++i) o = fmaf(wts[i * group + g], st[(i * group + g) * S + d], o);
-      if (last_round) {
-        a.out[((size_t)b * Hq + (size_t)h * group + g) * D + d] = o / wts[kWtsL + g];
+    for (int o = o_begin + tid; o < o_end; o += kCombineThreads) {
+      const int g = o / (D / 4), d4 = o - g * (D / 4);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!first) {
+        const float r = rowR[g];
+        const float4 v = reinterpret_cast<const float4*>(run + g * S)[d4];
+        acc = make_float4(v.x * r, v.y * r, v.z * r, v.w * r);
+      }
+#pragma unroll 8
+      for (int i = 0; i < n; ++i) {
+        const float w = pm[i * group + g];
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.partials + ((size_t)pieces[base + i] * group + g) * S) + d4);
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+      if (last) {
+        const float inv = 1.f / rowL[g];
+        float* dst = a.out + ((size_t)b * Hq + (size_t)h * group + g) * D + 4 * d4;
+        dst[0] = acc.x * inv;
+        dst[1] = acc.y * inv;
+        dst[2] = acc.z * inv;
+        dst[3] = acc.w * inv;
       } else {
-        run[g * S + d] = o;
+        reinterpret_cast<float4*>(run + g * S)[d4] = acc;
       }
     }
-    if (!last_round && tid < group) {
-      run[tid * S + D] = wts[kWtsM + tid];
-      run[tid * S + D + 1] = wts[kWtsL + tid];
-    }
     __syncthreads();
-    have_run = true;
   }
 }
 
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeArgs a) {
   constexpr int S = state_stride(D);
-  __shared__ __align__(16) float st[combine_stage<D>() * 8 * S];
-  __shared__ float wts[kWtsM + 8];
-  __shared__ __align__(16) float run[8 * S];  // running merged state between rounds
+  __shared__ float pm[kCombinePass * 8];
+  __shared__ float pl[kCombinePass * 8];
+  __shared__ __align__(16) float run[8 * S];  // running merged state between passes
+  __shared__ float rowv[24];
   __shared__ int pieces[kCombineMaxPieces];
   __shared__ int s_np;
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -345,28 +355,46 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeAr
   const long long W = *a.total;
   const long long P = a.num_ctas;
   const int alpha = a.seg_cost;
+  const int n_out = a.group * (D / 4);  // float4 outputs of a segment
   for (int c = 1 + blockIdx.x; c < P; c += gridDim.x) {
     const int4 d = a.desc[c];
     // empty range, or the boundary does not fall inside the segment's blocks
     if (d.x < 0 || d.z <= alpha) continue;
     // segment (d.x, d.y) starts at stream position S0 and is d.w positions
-    // long; it is merged by the iteration of the first boundary inside its
-    // blocks (CTAs with empty ranges may sit between: compare owners)
+    // long; its pieces belong to CTAs c_first .. c_last
     const long long S0 = range_begin(c, W, P) - d.z;
     const long long c_first = cta_of(S0 + alpha, W, P);
-    if (cta_of(range_begin(c, W, P) - 1, W, P) != c_first) continue;
     const long long c_last = cta_of(S0 + d.w - 1, W, P);
-    if (threadIdx.x == 0) {
-      int np = 0;
-      for (long long k = c_first; k <= c_last && np < kCombineMaxPieces; ++k) {
-        if (range_begin(k, W, P) == range_begin(k + 1, W, P)) continue;  // an empty range holds no piece
-        const int slot = (k == c_first && range_begin(k, W, P) < S0) ? 1 : 0;
-        pieces[np++] = (int)(k * 2 + slot);
+    int helper = 0, helpers = 1, np;
+    if (W >= P) {
+      // no empty ranges: every boundary inside the segment has a combine
+      // CTA, and they share the segment's outputs
+      helper = (int)(c - c_first - 1);
+      helpers = (int)(c_last - c_first);
+      np = (int)(c_last - c_first + 1);
+      const int slot_first = range_begin(c_first, W, P) < S0 ? 1 : 0;
+      for (int i = threadIdx.x; i < np && i < kCombineMaxPieces; i += kCombineThreads)
+        pieces[i] = (int)((c_first + i) * 2 + (i == 0 ? slot_first : 0));
+      np = min(np, kCombineMaxPieces);
+    } else {
+      // less work than CTAs (empty ranges hold no piece): the first boundary
+      // inside merges alone
+      if (cta_of(range_begin(c, W, P) - 1, W, P) != c_first) continue;
+      if (threadIdx.x == 0) {
+        int n = 0;
+        for (long long k = c_first; k <= c_last && n < kCombineMaxPieces; ++k) {
+          if (range_begin(k, W, P) == range_begin(k + 1, W, P)) continue;
+          pieces[n++] = (int)(k * 2 + ((k == c_first && range_begin(k, W, P) < S0) ? 1 : 0));
+        }
+        s_np = n;
       }
-      s_np = np;
+      __syncthreads();
+      np = s_np;
     }
     __syncthreads();
-    combine_segment<D>(a, d.x, d.y, pieces, s_np, st, wts, run);
+    const int o_begin = (int)((long long)helper * n_out / helpers);
+    const int o_end = (int)((long long)(helper + 1) * n_out / helpers);
+    combine_segment<D>(a, d.x, d.y, pieces, np, pm, pl, run, rowv, o_begin, o_end);
   }
   if constexpr (kTrace) {
     if (a.trace && threadIdx.x == 0) atomicMax(a.trace + 3, gtime());

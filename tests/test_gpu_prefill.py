@@ -32,9 +32,11 @@ def _case(dtype, hq, hkv, d, bs, prior, prompt, seed):
     T = int(sum(prompt))
     cu = np.concatenate([[0], np.cumsum(prompt)]).astype(np.int32)
     dev = torch.device("cuda", 0)
-    q = torch.randn((T, hq, d), device=dev).to(dtype)
-    k = torch.randn((T, hkv, d), device=dev).to(dtype)
-    v = torch.randn((T, hkv, d), device=dev).to(dtype)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    q = torch.randn((T, hq, d), device=dev, generator=gen).to(dtype)
+    k = torch.randn((T, hkv, d), device=dev, generator=gen).to(dtype)
+    v = torch.randn((T, hkv, d), device=dev, generator=gen).to(dtype)
     return dict(B=B, T=T, bt=bt, cu=cu, ctx=np.array(prior, np.int32), total=total, nb=nb, q=q, k=k, v=v)
 
 

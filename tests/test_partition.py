@@ -132,3 +132,35 @@ def test_partition_covers_every_block_once(seed, B, H, P, alpha):
             else:
                 assert complete == {False}
                 assert sorted(owners) == sorted(merged[(b, h)]), (b, h)
+
+
+@pytest.mark.parametrize("alpha", [0, 3])
+@pytest.mark.parametrize("seed,B,H,P", [(0, 8, 1, 296), (1, 128, 8, 296), (3, 64, 32, 444), (5, 256, 8, 296)])
+def test_combine_helpers_cover_each_split_segment_once(seed, B, H, P, alpha):
+    # work >= CTAs: the combine CTAs of all boundaries inside a split segment
+    # share its outputs [k n / helpers, (k + 1) n / helpers)
+    rng = np.random.default_rng(seed)
+    nblk = rng.integers(1, 3000, B)
+    W, pieces, _ = walk(nblk, H, P, alpha)
+    assert W >= P
+    seg = nblk + alpha
+    pre = np.concatenate([[0], np.cumsum(seg)])
+    n_out = 8 * 32
+    done = {}
+    for c in range(1, P):
+        lo = range_begin(c, W, P)
+        b = int(np.searchsorted(H * pre, lo, side="right") - 1)
+        r = lo - H * pre[b]
+        h, off = r // seg[b], r % seg[b]
+        if off <= alpha:
+            continue
+        s0 = lo - off
+        cf, cl = cta_of(s0 + alpha, W, P), cta_of(s0 + seg[b] - 1, W, P)
+        k, n_h = c - cf - 1, cl - cf
+        assert 0 <= k < n_h
+        done.setdefault((b, h), []).append((k * n_out // n_h, (k + 1) * n_out // n_h, n_h))
+    for key, parts in done.items():
+        parts.sort()
+        assert len(parts) == parts[0][2]  # every helper present
+        assert parts[0][0] == 0 and parts[-1][1] == n_out
+        assert all(parts[i][1] == parts[i + 1][0] for i in range(len(parts) - 1))
