@@ -710,6 +710,99 @@ def run_qkv(args) -> None:
     }))
 
 
+def run_prefill(args) -> None:
+    """`--op prefill`: causal prefill into the paged cache (clove_cuda_paged_prefill:
+    RoPE + cache write + attention) on one GPU, bf16, 32 query / 8 KV heads x
+    128, block 32, fresh prompts: `--batch` prompts of `--prompt` tokens
+    (default 8 x 2048).  FLOPs per step = batch * Hq * 2 * T^2 * D (QK^T and
+    P.V over the causal half).  Reports TFLOP/s against the measured bf16
+    tensor peak, and the warp-MMA kernel's time for comparison."""
+    import torch
+
+    from clove_b200 import KVPool, launch_count, set_decode_variant
+    ws, rank, local = _dist()
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    hq, hkv, D, bs = 32, 8, 128, 32
+    B, T = (args.batch or 8), args.prompt
+    need = (T + bs - 1) // bs
+    nb = B * need
+    g = torch.Generator(device=dev)
+    g.manual_seed(606)
+    pool = KVPool(nb, bs, hkv, D, torch.bfloat16, dev)
+    pool.storage.normal_(generator=g)
+    bt = torch.arange(nb, dtype=torch.int32, device=dev).reshape(B, need)
+    cu = torch.arange(0, (B + 1) * T, T, dtype=torch.int32, device=dev)
+    ctx = torch.zeros(B, dtype=torch.int32, device=dev)
+    q = torch.randn((B * T, hq, D), device=dev, generator=g).bfloat16()
+    k = torch.randn((B * T, hkv, D), device=dev, generator=g).bfloat16()
+    v = torch.randn((B * T, hkv, D), device=dev, generator=g).bfloat16()
+    flops = B * hq * 2.0 * T * T * D
+
+    def step():
+        return pool.prefill(q, k, v, cu, bt, ctx, max_ctx=T, rope_theta=10000.0)
+
+    def timed(n):
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            step()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    n0 = launch_count()
+    step()
+    torch.cuda.synchronize()
+    per_step = launch_count() - n0
+    with ClockSampler(local) as clk:
+        ms = timed(args.steps)
+    set_decode_variant("mma")
+    try:
+        ms_mma = timed(max(3, args.steps // 4))
+    finally:
+        set_decode_variant("auto")
+    assert pool.pool_status() == 0
+    # end to end: prompts from pinned host memory, outputs back to host
+    hq_, hk_, hv_ = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+    out_h = torch.empty((B * T, hq, D), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        q.copy_(hq_, non_blocking=True), k.copy_(hk_, non_blocking=True), v.copy_(hv_, non_blocking=True)
+        out_h.copy_(step(), non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ne = max(3, args.steps // 4)
+    e0.record()
+    for _ in range(ne):
+        q.copy_(hq_, non_blocking=True), k.copy_(hk_, non_blocking=True), v.copy_(hv_, non_blocking=True)
+        out_h.copy_(step(), non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / ne
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak, kind = (pk["bf16_tflops"], "measured burst") if "bf16_tflops" in pk else (1590.0, "fallback")
+    tf = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "paged prefill TFLOP/s (causal)", "value": tf, "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"prefill {B} x {T} tokens, 32q/8kv x 128, block 32, RoPE, fresh prompts",
+                   "l2": "K/V re-read from L2 by design (causal tiles)"},
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                     "traffic": None, "peak_kind": kind,
+                     "note": "whole call (RoPE + cache write + plan + attention) over the causal FLOPs"},
+        "warp_mma_ms_per_step": ms_mma, "warp_mma_tflops": flops / (ms_mma * 1e-3) / 1e12,
+        "e2e": {"value": flops / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": (q.numel() + k.numel() + v.numel()) * 2, "d2h_bytes_per_step": out_h.numel() * 4},
+        "gpu_launches": per_step * args.steps, "clocks": clk.summary(),
+    }), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -717,8 +810,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2")
-    ap.add_argument("--op", default="decode", choices=["decode", "qkv_append"],
-                    help="decode (the headline path) or the fused Q/K/V projection + append")
+    ap.add_argument("--op", default="decode", choices=["decode", "qkv_append", "prefill"],
+                    help="decode (the headline path), the fused Q/K/V projection + append, or prefill")
+    ap.add_argument("--prompt", type=int, default=2048, help="--op prefill: tokens per prompt")
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--batch", type=int, default=None, help="override the config batch (profiling only)")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a captured CUDA graph")
@@ -732,6 +826,8 @@ def main() -> None:
     args = ap.parse_args()
     if args.op == "qkv_append":
         run_qkv(args)
+    elif args.op == "prefill":
+        run_prefill(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
