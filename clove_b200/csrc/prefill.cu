@@ -40,6 +40,7 @@ struct PrefillPrepArgs {
   int32_t* flags;
   int batch, num_tokens, hq, hkv, D, bs, bt_stride, num_blocks, max_ctx;
   float rope_theta;       // 0: no rotation
+  int write_rows;         // 1: fill row_tables / row_lens (the decode-reuse path reads them)
 };
 
 template <typename T>
@@ -68,9 +69,29 @@ __device__ void rope_row(const T* in, T* out, int D, int pos, float theta, int l
   }
 }
 
-// One CTA per prompt token.
+// Rotate 8 consecutive elements (4 adjacent pairs starting at pair i0) of a
+// 16-byte vector with the token's per-pair (cos, sin).
+template <typename T>
+__device__ __forceinline__ uint4 rope8(uint4 in, const float* cs, const float* sn, int i0) {
+  const T* x = reinterpret_cast<const T*>(&in);
+  uint4 out;
+  T* y = reinterpret_cast<T*>(&out);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float x0 = Elem<T>::to_f(x[2 * j]), x1 = Elem<T>::to_f(x[2 * j + 1]);
+    y[2 * j] = from_f<T>(x0 * cs[i0 + j] - x1 * sn[i0 + j]);
+    y[2 * j + 1] = from_f<T>(x0 * sn[i0 + j] + x1 * cs[i0 + j]);
+  }
+  return out;
+}
+
+// One CTA per prompt token (16-bit pools; f32 pools take rope_row below).
+// The token's rotation angles, pos * theta^(-2i/D) for pair i (the pairing of
+// src/lazy.rs:4834-4842), are computed once into shared memory and applied to
+// every head with 16-byte loads and stores.
 template <typename T>
 __global__ void __launch_bounds__(128) prefill_prep_kernel(const PrefillPrepArgs p) {
+  __shared__ float cs[128], sn[128];  // D / 2 <= 128
   const int t = blockIdx.x;
   // sequence of token t: largest b with cu_seqlens[b] <= t
   int lo = 0, hi = p.batch - 1;
@@ -82,18 +103,73 @@ __global__ void __launch_bounds__(128) prefill_prep_kernel(const PrefillPrepArgs
   const int pos = __ldg(p.context_lens + b) + (t - __ldg(p.cu_seqlens + b));
   const int32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
   const bool in_range = pos >= 0 && pos < p.max_ctx && pos / p.bs < p.bt_stride;
-  // expanded table row and length
-  for (int j = threadIdx.x; j < p.bt_stride; j += blockDim.x) p.row_tables[(size_t)t * p.bt_stride + j] = bt[j];
-  if (threadIdx.x == 0) {
-    p.row_lens[t] = in_range ? pos + 1 : 0;
-    if (!in_range) atomicOr(p.flags, CLOVE_FLAG_CTX_RANGE);
+  if (p.write_rows) {
+    // expanded table row and length (the decode-reuse path treats every
+    // prompt token as a decode row)
+    for (int j = threadIdx.x; j < p.bt_stride; j += blockDim.x) p.row_tables[(size_t)t * p.bt_stride + j] = bt[j];
+    if (threadIdx.x == 0) p.row_lens[t] = in_range ? pos + 1 : 0;
   }
+  if (threadIdx.x == 0 && !in_range) atomicOr(p.flags, CLOVE_FLAG_CTX_RANGE);
+  const bool rot = p.rope_theta > 0.f;
+  if (rot) {
+    for (int i = threadIdx.x; i < p.D / 2; i += blockDim.x) {
+      const float ang = (float)pos * powf(p.rope_theta, -2.f * (float)i / (float)p.D);
+      sincosf(ang, &sn[i], &cs[i]);
+    }
+    __syncthreads();
+  }
+  constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte vector
+  const int vpr = p.D / EPV;                // vectors per head row
   // rotated query rows
+  {
+    const uint4* qs = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (size_t)t * p.hq * p.D);
+    uint4* qd = reinterpret_cast<uint4*>(static_cast<T*>(p.q_rot) + (size_t)t * p.hq * p.D);
+    for (int u = threadIdx.x; u < p.hq * vpr; u += blockDim.x) {
+      const uint4 x = __ldg(qs + u);
+      qd[u] = rot ? rope8<T>(x, cs, sn, (u % vpr) * (EPV / 2)) : x;
+    }
+  }
+  if (!in_range) return;
+  // K (rotated) and V into the slot
+  const int phys = __ldg(bt + pos / p.bs);
+  if (phys < 0 || phys >= p.num_blocks) {
+    if (threadIdx.x == 0) atomicOr(p.flags, CLOVE_FLAG_BLOCK_OOB);
+    return;
+  }
+  const size_t row = ((size_t)phys * p.bs + pos % p.bs) * p.hkv * p.D;
+  const uint4* ks = reinterpret_cast<const uint4*>(static_cast<const T*>(p.k) + (size_t)t * p.hkv * p.D);
+  const uint4* vs = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v) + (size_t)t * p.hkv * p.D);
+  uint4* kc = reinterpret_cast<uint4*>(static_cast<T*>(p.k_cache) + row);
+  uint4* vc = reinterpret_cast<uint4*>(static_cast<T*>(p.v_cache) + row);
+  for (int u = threadIdx.x; u < p.hkv * vpr; u += blockDim.x) {
+    const uint4 x = __ldg(ks + u);
+    kc[u] = rot ? rope8<T>(x, cs, sn, (u % vpr) * (EPV / 2)) : x;
+    vc[u] = __ldg(vs + u);
+  }
+}
+
+// f32 pools: the same with element-wise rotation.
+__global__ void __launch_bounds__(128) prefill_prep_f32_kernel(const PrefillPrepArgs p) {
+  using T = float;
+  const int t = blockIdx.x;
+  int lo = 0, hi = p.batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(p.cu_seqlens + mid) <= t) lo = mid; else hi = mid - 1;
+  }
+  const int b = lo;
+  const int pos = __ldg(p.context_lens + b) + (t - __ldg(p.cu_seqlens + b));
+  const int32_t* bt = p.block_tables + (size_t)b * p.bt_stride;
+  const bool in_range = pos >= 0 && pos < p.max_ctx && pos / p.bs < p.bt_stride;
+  if (p.write_rows) {
+    for (int j = threadIdx.x; j < p.bt_stride; j += blockDim.x) p.row_tables[(size_t)t * p.bt_stride + j] = bt[j];
+    if (threadIdx.x == 0) p.row_lens[t] = in_range ? pos + 1 : 0;
+  }
+  if (threadIdx.x == 0 && !in_range) atomicOr(p.flags, CLOVE_FLAG_CTX_RANGE);
   const T* qs = static_cast<const T*>(p.q) + (size_t)t * p.hq * p.D;
   T* qd = static_cast<T*>(p.q_rot) + (size_t)t * p.hq * p.D;
   for (int h = 0; h < p.hq; ++h) rope_row<T>(qs + h * p.D, qd + h * p.D, p.D, pos, p.rope_theta, threadIdx.x, blockDim.x);
   if (!in_range) return;
-  // K (rotated) and V into the slot
   const int phys = __ldg(bt + pos / p.bs);
   if (phys < 0 || phys >= p.num_blocks) {
     if (threadIdx.x == 0) atomicOr(p.flags, CLOVE_FLAG_BLOCK_OOB);
@@ -158,6 +234,11 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, co
     set_last_error("paged_prefill: null pointer or workspace not 256-byte aligned");
     return CLOVE_ERR_INVALID_ARG;
   }
+  if (pool->elem_bytes == 2 && ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                                 reinterpret_cast<uintptr_t>(v)) & 15u)) {
+    set_last_error("paged_prefill: q, k, v must be 16-byte aligned");
+    return CLOVE_ERR_INVALID_ARG;
+  }
   if (num_q_heads % pool->num_kv_heads || (long long)max_ctx > (long long)bt_stride * pool->block_size) {
     set_last_error("paged_prefill: num_q_heads / max_ctx inconsistent with the pool and tables");
     return CLOVE_ERR_INVALID_ARG;
@@ -194,9 +275,15 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, co
   p.num_blocks = pool->num_blocks;
   p.max_ctx = max_ctx;
   p.rope_theta = rope_theta;
+  // the expanded per-token tables are read only by the decode-reuse path
+  const bool tc_path = decode_variant() == 0 && prefill_tc_supported(*pool, num_q_heads);
+  const bool mma_path = decode_variant() != 1 && pool->elem_bytes == 2 && pool->has_swizzled &&
+                        pool->block_size >= 8 && num_q_heads / pool->num_kv_heads <= 16 &&
+                        (pool->head_dim == 64 || pool->head_dim == 128);
+  p.write_rows = (tc_path || mma_path) ? 0 : 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (pool->dtype) {
-    case CLOVE_DTYPE_F32: prefill_prep_kernel<float><<<num_tokens, 128, 0, s>>>(p); break;
+    case CLOVE_DTYPE_F32: prefill_prep_f32_kernel<<<num_tokens, 128, 0, s>>>(p); break;
     case CLOVE_DTYPE_BF16: prefill_prep_kernel<__nv_bfloat16><<<num_tokens, 128, 0, s>>>(p); break;
     default: prefill_prep_kernel<__half><<<num_tokens, 128, 0, s>>>(p); break;
   }

@@ -47,9 +47,11 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillArgs p) {
   }
   __syncthreads();
   const int maxk = s_maxk;
-  for (int b = tid; b < p.batch; b += blockDim.x) {
-    const int len = p.cu_seqlens[b + 1] - p.cu_seqlens[b], ctx = p.context_lens[b];
-    for (int j = 0; j * p.tq < len; ++j)
+  // a sequence's tiles are spread over all threads (few long prompts are
+  // the common prefill batch)
+  for (int b = 0; b < p.batch; ++b) {
+    const int len = __ldg(p.cu_seqlens + b + 1) - __ldg(p.cu_seqlens + b), ctx = __ldg(p.context_lens + b);
+    for (int j = tid; j * p.tq < len; j += blockDim.x)
       atomicAdd(&hist[(int)((long long)(keys_of(b, j, len, ctx) - 1) * kPfBins / maxk)], 1);
   }
   __syncthreads();
@@ -63,9 +65,9 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(PrefillArgs p) {
     *p.n_items = acc;
   }
   __syncthreads();
-  for (int b = tid; b < p.batch; b += blockDim.x) {
-    const int len = p.cu_seqlens[b + 1] - p.cu_seqlens[b], ctx = p.context_lens[b];
-    for (int j = 0; j * p.tq < len; ++j) {
+  for (int b = 0; b < p.batch; ++b) {
+    const int len = __ldg(p.cu_seqlens + b + 1) - __ldg(p.cu_seqlens + b), ctx = __ldg(p.context_lens + b);
+    for (int j = tid; j * p.tq < len; j += blockDim.x) {
       const int bin = (int)((long long)(keys_of(b, j, len, ctx) - 1) * kPfBins / maxk);
       p.items[base[bin] + atomicAdd(&hist[bin], 1)] = make_int2(b, j);
     }

@@ -25,10 +25,11 @@
 //   O += P V    tcgen05.mma, M 128 x N 128 dims x K 128 keys, P K-major and V
 //               MN-major (the cache rows are dim-contiguous), O in tensor
 //               memory for the whole unit.
-// Roles (192 threads): warp 0 issues the bulk tensor copies (Q once per unit;
+// Roles (320 threads): warp 0 issues the bulk tensor copies (Q once per unit;
 // K and V of each step as [block_size, 64] boxes per 64-dim half), warp 1
-// issues the MMAs and owns the tensor-memory allocation, warps 2-5 run the
-// softmax and the epilogue (thread r owns tensor-memory lane r = row r).  S
+// issues the MMAs and owns the tensor-memory allocation, warps 2-9 run the
+// softmax and the epilogue (two warpgroups: row r = tensor-memory lane r,
+// each warpgroup on 64 of the row's key columns and of O's dims).  S
 // of step s+1 is computed while the softmax of step s runs and P.V of step s
 // waits for its P.  Every wait is bounded; a wait that runs out sets
 // CLOVE_FLAG_TIMEOUT and the CTA winds down without hanging.
@@ -49,7 +50,8 @@ namespace clove {
 
 namespace {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
+constexpr int kSoftThreads = 256;  // two warpgroups, each on 64 of a row's 128 key columns
 constexpr int kTcRows = 128;                            // query rows per unit (MMA M)
 constexpr int kTcKeys = 128;                            // keys per step
 constexpr int kTcD = 128;                               // head_dim
@@ -62,6 +64,7 @@ constexpr uint32_t kPBytes = kTcRows * kTcKeys * 2;     // 32 KB
 constexpr uint32_t kSmemBytes = kQBytes + kStages * kStageBytes + 2 * kPBytes + 1024;
 constexpr uint32_t kTmemCols = 512;                     // S buffers at columns 0 and 128, O at 256
 constexpr uint32_t kTmemO = 256;
+constexpr uint32_t kTmemX = 384;                        // row max / sum exchange between the two softmax halves
 
 struct TcUnit {
   int b, j, h, nkeys, nsteps, valid;
@@ -77,6 +80,18 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// One 32-bit column of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(__float_as_uint(v)) : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  tmem_ld_wait();
+  return __uint_as_float(r);
+}
 
 // A whole 128-column row of this thread's lane.
 __device__ __forceinline__ void tmem_ld_row128(uint32_t taddr, float (&v)[128]) {
@@ -118,11 +133,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
   __shared__ __align__(8) uint64_t q_full, q_empty, o_empty, drain;
-  __shared__ __align__(8) uint64_t kv_full[kStages], kv_empty[kStages], s_full[2], s_empty[2], p_full[2];
+  // K and V of a stage are filled and released separately: K is free again
+  // once that step's S MMAs finish, V once its P.V finishes
+  __shared__ __align__(8) uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+  __shared__ __align__(8) uint64_t s_full[2], s_empty[2], p_full[2];
   // P.V of P index i completes phase i / 2 of pv_done[i % 2]: a waiter is never more than one phase
   // behind (the next completion on that barrier needs a P the waiter has not produced yet)
   __shared__ __align__(8) uint64_t pv_done[2];
   __shared__ __align__(8) uint64_t ufull[2], uempty[2];
+  __shared__ __align__(8) uint64_t pair_bar[4];  // the two softmax warps on one lane quarter
   __shared__ TcUnit slots[2];
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
@@ -139,19 +158,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
     mbar_init(&q_empty, 1);
-    mbar_init(&o_empty, kTcRows);
+    mbar_init(&o_empty, kSoftThreads);
     mbar_init(&drain, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 64);
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kTcRows);
-      mbar_init(&p_full[i], kTcRows);
+      mbar_init(&s_empty[i], kSoftThreads);
+      mbar_init(&p_full[i], kSoftThreads);
       mbar_init(&pv_done[i], 1);
       mbar_init(&ufull[i], 1);
-      mbar_init(&uempty[i], 1 + kTcRows / 32);  // the MMA thread + one arrival per softmax warp
+      mbar_init(&uempty[i], 1 + kSoftThreads / 32);  // the MMA thread + one arrival per softmax warp
     }
     abort_flag = 0;
     fence_barrier_init();
@@ -251,22 +273,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) phys[i] = __shfl_sync(0xffffffffu, cur, i);
         if (lane == 0) {
-          if (!wait(&kv_empty[st], ((uint32_t)(g / kStages) & 1u) ^ 1u)) {
+          const uint32_t par = ((uint32_t)(g / kStages) & 1u) ^ 1u;
+          const uint32_t bytes = (uint32_t)nb * (uint32_t)bs * 128u * 2u;  // two 64-dim halves
+          unsigned char* kst = sKV + (size_t)st * kStageBytes;
+          unsigned char* vst = kst + kKVBytes;
+          if (!wait(&k_empty[st], par)) {
             ok = false;
           } else if (a.inject_stall && u == 0 && s == 0) {
-            // test hook: this step is never filled, so the MMA warp's wait runs out
+            // test hook: this step's K is never filled, so the MMA warp's wait runs out
           } else {
-            mbar_arrive_expect_tx(&kv_full[st], (uint32_t)nb * (uint32_t)bs * 128u * 4u);
-            unsigned char* kst = sKV + (size_t)st * kStageBytes;
-            unsigned char* vst = kst + kKVBytes;
+            {
+              mbar_arrive_expect_tx(&k_full[st], bytes);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              if (i < nb) {
-                const uint32_t row = (uint32_t)(i * bs) * 128u;
-                tma_load_3d(kst + row, &tm_k, &kv_full[st], 0, x.h, phys[i] * bs, pol);
-                tma_load_3d(kst + kHalfBytes + row, &tm_k, &kv_full[st], 64, x.h, phys[i] * bs, pol);
-                tma_load_3d(vst + row, &tm_v, &kv_full[st], 0, x.h, phys[i] * bs, pol);
-                tma_load_3d(vst + kHalfBytes + row, &tm_v, &kv_full[st], 64, x.h, phys[i] * bs, pol);
+              for (int i = 0; i < 16; ++i) {
+                if (i < nb) {
+                  const uint32_t row = (uint32_t)(i * bs) * 128u;
+                  tma_load_3d(kst + row, &tm_k, &k_full[st], 0, x.h, phys[i] * bs, pol);
+                  tma_load_3d(kst + kHalfBytes + row, &tm_k, &k_full[st], 64, x.h, phys[i] * bs, pol);
+                }
+              }
+            }
+          }
+          if (ok && !wait(&v_empty[st], par)) {
+            ok = false;
+          } else if (ok) {
+            {
+              mbar_arrive_expect_tx(&v_full[st], bytes);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                if (i < nb) {
+                  const uint32_t row = (uint32_t)(i * bs) * 128u;
+                  tma_load_3d(vst + row, &tm_v, &v_full[st], 0, x.h, phys[i] * bs, pol);
+                  tma_load_3d(vst + kHalfBytes + row, &tm_v, &v_full[st], 64, x.h, phys[i] * bs, pol);
+                }
               }
             }
           }
@@ -279,9 +318,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       // drain: copies in flight must land before the CTA exits
       for (int t = max(0, g - kStages); t < g; ++t) {
+        for (uint32_t i = 0; i < a.wait_limit; ++i)
+          if (mbar_try_wait(&v_full[t % kStages], (uint32_t)(t / kStages) & 1u)) break;
         if (a.inject_stall && t == stalled_g) continue;
         for (uint32_t i = 0; i < a.wait_limit; ++i)
-          if (mbar_try_wait(&kv_full[t % kStages], (uint32_t)(t / kStages) & 1u)) break;
+          if (mbar_try_wait(&k_full[t % kStages], (uint32_t)(t / kStages) & 1u)) break;
       }
       if (ui > 0)
         for (uint32_t i = 0; i < a.wait_limit; ++i)
@@ -305,7 +346,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (s < x.nsteps) {
             const int st = (g + s) % kStages;
             const int sb = sc & 1;
-            if (!wait(&kv_full[st], (uint32_t)((g + s) / kStages) & 1u) ||
+            if (!wait(&k_full[st], (uint32_t)((g + s) / kStages) & 1u) ||
                 !wait(&s_empty[sb], ((uint32_t)(sc >> 1) & 1u) ^ 1u)) {
               ok = false;
               break;
@@ -319,6 +360,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 umma_f16(tmem + (uint32_t)(sb * kTcKeys), sw128_kmajor_desc(qa + c * (kQBytes / 2)) + 2 * k,
                          sw128_kmajor_desc(ka + c * kHalfBytes) + 2 * k, idesc_s, (c | k) ? 1u : 0u);
             umma_commit(&s_full[sb]);
+            umma_commit(&k_empty[st]);  // K of this stage is free once S completes
             ++sc;
             if (s == x.nsteps - 1) umma_commit(&q_empty);  // Q is free once these complete
           }
@@ -326,7 +368,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int t = s - 1;
             const int st = (g + t) % kStages;
             const int pb = pc & 1;
-            if (!wait(&p_full[pb], (uint32_t)(pc >> 1) & 1u) ||
+            if (!wait(&p_full[pb], (uint32_t)(pc >> 1) & 1u) || !wait(&v_full[st], (uint32_t)((g + t) / kStages) & 1u) ||
                 (t == 0 && !wait(&o_empty, ((uint32_t)ui & 1u) ^ 1u))) {
               ok = false;
               break;
@@ -341,7 +383,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 umma_f16(tmem + kTmemO, sw128_kmajor_desc(pa + c * (kPBytes / 2)) + 2 * k,
                          sw128_mnmajor_desc(va + (uint32_t)(64 * c + 16 * k) * 128u, kHalfBytes, 1024), idesc_pv,
                          (t == 0 && c == 0 && k == 0) ? 0u : 1u);
-            umma_commit(&kv_empty[st]);
+            umma_commit(&v_empty[st]);
             umma_commit(&pv_done[pb]);
             ++pc;
           }
@@ -357,10 +399,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax + epilogue
+    // Warps 2-9: warp w reads tensor-memory lanes 32 (w % 4) .. (its rows);
+    // warps w and w + 4 share those rows, warp 2-5 taking key columns 0-63
+    // and dims 0-63 of O, warps 6-9 columns 64-127 and dims 64-127.  The two
+    // halves of a row exchange their maxima each step (a pairwise named
+    // barrier) and their sums once per unit.
     const int r = (warp & 3) * 32 + lane;  // this thread's row = tensor-memory lane
+    const int half = (warp - 2) >> 2;      // 0: columns 0-63, 1: columns 64-127
+    const int col0 = 64 * half;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    uint64_t* pbar = &pair_bar[warp & 3];  // the pair of warps on these rows
+    uint32_t pphase = 0;
     const int t_in = r / G, gq = r - (r / G) * G;
-    int ui = 0, g = 0, sc = 0, pc = 0;
+    // exchange columns: kTmemX + 2 parity + half (maxima, by step parity), kTmemX + 4 + half (sums)
+    const uint32_t xcol = tmem + lane_off + kTmemX;
+    int ui = 0, g = 0, sc = 0, pc = 0, st_par = 0;
     // Waits here are warp-uniform: the tensor-memory loads and stores that
     // follow are warp-collective (.sync.aligned), so no lane may leave early.
     auto wait_w = [&](uint64_t* bar, uint32_t parity) -> bool {
@@ -370,6 +423,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // wait until P.V of P index i has completed (i < 0: nothing to wait for)
     auto pv_wait = [&](int i) -> bool {
       return i < 0 || wait_w(&pv_done[i & 1], (uint32_t)(i >> 1) & 1u);
+    };
+    // The two warps of a row pair meet (bounded, like every wait here: a
+    // partner that left on an abort makes this return false, never hang).
+    auto pair_sync = [&]() -> bool {
+      tc_fence_before();
+      mbar_arrive(pbar);
+      const bool r = wait_w(pbar, pphase);
+      pphase ^= 1u;
+      tc_fence_after();
+      return r;
     };
     bool ok = true;
     while (ok) {
@@ -392,37 +455,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         tc_fence_after();
-        float v[128];
-        tmem_ld_row128(tmem + lane_off + (uint32_t)(sb * kTcKeys), v);
+        float v[64];
+        {
+          uint32_t rr[4][16];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) tmem_ld16_async(tmem + lane_off + (uint32_t)(sb * kTcKeys + col0 + 16 * i), rr[i]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int k = 0; k < 16; ++k) v[16 * i + k] = __uint_as_float(rr[i][k]);
+        }
         tc_fence_before();
         mbar_arrive(&s_empty[sb]);
         ++sc;
-        const int key0 = s * kTcKeys;
-        // row max of the raw scores (the scale is positive); the causal mask
-        // only on steps that reach past this row's position
+        const int key0 = s * kTcKeys + col0;
+        // this half's max of the raw scores (the scale is positive); the
+        // causal mask only on steps that reach past this row's position
         float mx = -INFINITY;
-        if (key0 + kTcKeys - 1 <= pos) {
+        if (key0 + 63 <= pos) {
 #pragma unroll
-          for (int k = 0; k < kTcKeys; ++k) mx = fmaxf(mx, v[k]);
+          for (int k = 0; k < 64; ++k) mx = fmaxf(mx, v[k]);
         } else {
 #pragma unroll
-          for (int k = 0; k < kTcKeys; ++k) {
+          for (int k = 0; k < 64; ++k) {
             v[k] = key0 + k <= pos ? v[k] : -INFINITY;
             mx = fmaxf(mx, v[k]);
           }
         }
-        mx *= a.qscale;  // log2 domain
+        tmem_st1(xcol + 2 * st_par + half, mx);
+        if (!pair_sync()) {
+          ok = false;
+          break;
+        }
+        mx = fmaxf(mx, tmem_ld1(xcol + 2 * st_par + (half ^ 1))) * a.qscale;  // the row's max, log2 domain
+        st_par ^= 1;
         // P is taken relative to a reference m that moves only when the row's
         // max rises by more than 8 (log2 units): P <= 2^8 stays exact enough
         // in 16 bits and the sums in f32, and O is rescaled (a wait on the
-        // previous P.V) only on those rare jumps.
+        // previous P.V) only on those rare jumps.  Both halves of a row see
+        // the same maxima, so they take the same decisions.
         const bool move = mx > m + 8.f;  // also true on the first visible key (m = -inf)
         const float m_new = move ? mx : m;
         const float ref = m_new == -INFINITY ? 0.f : m_new;
         const float corr = move ? exp2f(m - ref) : 1.f;  // 0 when m was -inf
         float rs = 0.f;
 #pragma unroll
-        for (int k = 0; k < kTcKeys; ++k) {
+        for (int k = 0; k < 64; ++k) {
           v[k] = ex2_approx(fmaf(v[k], a.qscale, -ref));
           rs += v[k];
         }
@@ -435,16 +514,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         {
-          unsigned char* prow = sP + (size_t)(pc & 1) * kPBytes + (size_t)r * 128;
+          unsigned char* prow = sP + (size_t)(pc & 1) * kPBytes + (size_t)half * (kPBytes / 2) + (size_t)r * 128;
 #pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int c = u >> 3, w = u & 7;
+          for (int w = 0; w < 8; ++w) {
             uint4 q4;
-            q4.x = pack2<T>(v[8 * u + 0], v[8 * u + 1]);
-            q4.y = pack2<T>(v[8 * u + 2], v[8 * u + 3]);
-            q4.z = pack2<T>(v[8 * u + 4], v[8 * u + 5]);
-            q4.w = pack2<T>(v[8 * u + 6], v[8 * u + 7]);
-            *reinterpret_cast<uint4*>(prow + (size_t)c * (kPBytes / 2) + ((w ^ (r & 7)) << 4)) = q4;
+            q4.x = pack2<T>(v[8 * w + 0], v[8 * w + 1]);
+            q4.y = pack2<T>(v[8 * w + 2], v[8 * w + 3]);
+            q4.z = pack2<T>(v[8 * w + 4], v[8 * w + 5]);
+            q4.w = pack2<T>(v[8 * w + 6], v[8 * w + 7]);
+            *reinterpret_cast<uint4*>(prow + ((w ^ (r & 7)) << 4)) = q4;
           }
         }
         if (__any_sync(0xffffffffu, rescale ? 1 : 0)) {
@@ -457,29 +535,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc_fence_after();
           const float f = rescale ? corr : 1.f;
 #pragma unroll 1
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < 4; ++i) {
             float t16[16];
-            tmem_ld16(tmem + lane_off + kTmemO + 16 * i, t16);
+            tmem_ld16(tmem + lane_off + kTmemO + col0 + 16 * i, t16);
 #pragma unroll
             for (int k = 0; k < 16; ++k) t16[k] *= f;
-            tmem_st16(tmem + lane_off + kTmemO + 16 * i, t16);
+            tmem_st16(tmem + lane_off + kTmemO + col0 + 16 * i, t16);
           }
         }
-        if (s == x.nsteps - 1 && key0 + kTcKeys > x.nkeys) {
+        if (s == x.nsteps - 1 && s * kTcKeys + kTcKeys > x.nkeys) {
           // V rows past the last key may hold any bits (P is 0 there, but
-          // 0 * NaN is NaN inside the MMA): zero them once the copies landed
+          // 0 * NaN is NaN inside the MMA): zero them once the copies landed;
+          // thread (row r, half) clears key row r's dims of its half
           const int st = (g + s) % kStages;
-          if (!wait_w(&kv_full[st], (uint32_t)((g + s) / kStages) & 1u)) {
+          if (!wait_w(&v_full[st], (uint32_t)((g + s) / kStages) & 1u)) {
             ok = false;
             break;
           }
-          if (key0 + r >= x.nkeys) {
-            unsigned char* vst = sKV + (size_t)st * kStageBytes + kKVBytes + (size_t)r * 128;
+          if (s * kTcKeys + r >= x.nkeys) {
+            unsigned char* vst = sKV + (size_t)st * kStageBytes + kKVBytes + (size_t)half * kHalfBytes + (size_t)r * 128;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              *reinterpret_cast<uint4*>(vst + u * 16) = make_uint4(0, 0, 0, 0);
-              *reinterpret_cast<uint4*>(vst + kHalfBytes + u * 16) = make_uint4(0, 0, 0, 0);
-            }
+            for (int u = 0; u < 8; ++u) *reinterpret_cast<uint4*>(vst + u * 16) = make_uint4(0, 0, 0, 0);
           }
         }
         fence_proxy_async_shared();  // P (and zeroed V rows) visible to the tensor cores
@@ -488,16 +564,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ++pc;
       }
       if (!ok) break;
-      // ---- epilogue: O / l for valid rows ----
+      // ---- epilogue: O / l for valid rows, this half's 64 dims ----
+      tmem_st1(xcol + 4 + half, l);
+      if (!pair_sync()) break;
+      const float lt = l + tmem_ld1(xcol + 4 + (half ^ 1));
       if (!pv_wait(pc - 1)) break;
       tc_fence_after();
       {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        float* dst = a.out + ((size_t)(seq0 + x.j * TQ + t_in) * a.hq + (size_t)x.h * G + gq) * kTcD;
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        float* dst = a.out + ((size_t)(seq0 + x.j * TQ + t_in) * a.hq + (size_t)x.h * G + gq) * kTcD + col0;
 #pragma unroll 1
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
           float o[16];
-          tmem_ld16(tmem + lane_off + kTmemO + 16 * i, o);
+          tmem_ld16(tmem + lane_off + kTmemO + col0 + 16 * i, o);
           if (row_ok) {
 #pragma unroll
             for (int k = 0; k < 16; k += 4)
