@@ -599,7 +599,7 @@ def run_qkv(args) -> None:
     """`--op qkv_append`: the fused Q/K/V projection + KV append
     (clove_cuda_qkv_append) on one GPU, shaped like config C3's decode step
     (hidden 4096 = 32 x 128, 32 q / 8 kv heads, bf16, batch 128 unless
-    --batch).  Four packed weight copies rotate (201 MB > L2), so each step
+    --batch; --hidden H gives H/128 q heads).  Four packed weight copies rotate (201 MB > L2), so each step
     streams its weights from HBM.  Reports the kernel's weight-streaming
     bandwidth against the measured HBM peak, and the same step done as a
     cuBLAS GEMM + the append kernel for comparison."""
@@ -611,7 +611,8 @@ def run_qkv(args) -> None:
         return
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    hidden, hq, hkv, D, bs = 4096, 32, 8, 128, 16
+    hidden = args.hidden or 4096
+    hq, hkv, D, bs = hidden // 128, 8, 128, 16
     B = args.batch or 128
     n_out = (hq + 2 * hkv) * D
     g = torch.Generator(device=dev)
@@ -813,6 +814,7 @@ def main() -> None:
     ap.add_argument("--op", default="decode", choices=["decode", "qkv_append", "prefill"],
                     help="decode (the headline path), the fused Q/K/V projection + append, or prefill")
     ap.add_argument("--prompt", type=int, default=2048, help="--op prefill: tokens per prompt")
+    ap.add_argument("--hidden", type=int, default=None, help="--op qkv_append: model width (default 4096)")
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--batch", type=int, default=None, help="override the config batch (profiling only)")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a captured CUDA graph")

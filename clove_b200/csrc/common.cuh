@@ -86,6 +86,16 @@ __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start before the previous kernel on the stream has
+// finished; griddep_wait blocks the calling thread until that kernel has
+// completed and its writes are visible.  griddep_launch_dependents lets the
+// next such kernel be scheduled (it still waits before reading anything).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
                : "memory");
@@ -244,7 +254,9 @@ struct DecodeArgs {
 //   griddepcontrol.wait, 2 producer done, 3 last consumer done;
 //   [kTraceUnit + 3 u + k]: piece u = 16 cta + (piece index within the
 //   CTA, < 16) k = 0 posted, 1 merged, 2 (cta << 32) | blocks.  Times from
-//   %globaltimer (ns).
+//   %globaltimer (ns).  The Q/K/V projection kernels use [kTraceCta + 8 cta
+//   + k]: k = 0 entry, 1 producer past griddepcontrol.wait, 2 first stage
+//   landed, 3 last MMA issued, 4 epilogue done.
 #ifdef CLOVE_TRACE
 constexpr bool kTrace = true;
 #else

@@ -596,6 +596,7 @@ void set_phase_timing(int on) { g_phase_timing.store(on ? 1 : 0); }
 
 static std::atomic<unsigned long long*> g_trace{nullptr};
 void set_trace_buffer(void* buf) { g_trace.store(static_cast<unsigned long long*>(buf)); }
+unsigned long long* trace_buffer() { return g_trace.load(); }
 
 int read_phase_ms(float* plan_ms, float* decode_ms, float* combine_ms) {
   std::lock_guard<std::mutex> lk(g_phase_mu);

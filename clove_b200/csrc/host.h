@@ -118,5 +118,6 @@ int debug_inject_stall();
 void set_phase_timing(int on);  // decode_kernels.cu
 int read_phase_ms(float* plan_ms, float* decode_ms, float* combine_ms);
 void set_trace_buffer(void* buf);  // decode_kernels.cu
+unsigned long long* trace_buffer();
 
 }  // namespace clove

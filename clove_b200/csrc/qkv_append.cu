@@ -49,6 +49,7 @@
 // the CTA finishes without hanging.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -66,7 +67,10 @@ namespace {
 constexpr int kQkvThreads = 192;  // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
 constexpr int kEpiThreads = 128;
 constexpr int kClusterThreads = 256;  // cluster schedule: warp 0 copies, warp 1 MMAs, all 8 in the epilogue
-constexpr int kStreamKMaxTile = 32;   // batch tiles up to this always use stream-K (see plan_qkv)
+constexpr int kStreamMaxBatch = 32;   // batches up to this use the stream-K kernel (its M is 128 rows)
+constexpr int kStreamM = 128;         // stream-K: batch rows per tile (MMA M)
+constexpr int kStreamN = 256;         // stream-K: output features per tile (MMA N)
+constexpr int kMaxHeadDim = 256;
 constexpr size_t kRingBudget = 200 * 1024;  // cluster schedule: ring bytes (its epilogue buffers overlay it)
 constexpr int kTileN = 128;       // output features per tile (tensor-core M)
 constexpr int kTileK = 64;        // hidden elements per stage (one 128-byte swizzle row)
@@ -83,29 +87,29 @@ struct QkvArgs {
   void* k_cache;
   void* v_cache;
   int32_t* flags;
-  float* partials;              // [tiles][max_contrib][128][batch_tile] f32
+  float* partials;              // stream-K: [tiles][max_contrib][16 chunks][4][batch_tile] float4
   int32_t* counters;            // [tiles], zero between calls
   int M, hidden, hq, hkv, D, bs, bt_stride, num_blocks;
   int n_out;        // (hq + 2 hkv) * D
   int kb_total;     // K blocks per tile
-  int ntiles_n;     // feature tiles
-  int batch_tile;   // MMA N (multiple of 16)
+  int ntiles_n;     // packed 128-feature chunks
+  int batch_tile;   // batch rows per tile, a multiple of 16 (cluster schedule: the MMA N)
   int nstage;
   int max_contrib;  // partial slots per tile
   int splits;       // cluster schedule: K splits (cluster size)
-  int acc_cols;     // tensor-memory columns per accumulator (power of two >= 32)
-  long long units;  // tiles * kb_total
+  long long units;  // stream-K: 256-feature tiles * kb_total
   float rope_theta;
   uint32_t wait_limit;
   int inject_stall;  // test hook: the first stage of the first CTA is never filled
+  unsigned long long* trace;  // timeline buffer (trace builds only; null otherwise)
 };
 
 // Instruction descriptor, kind::f16: f32 accumulate (bits 4-5 = 1), A and B
 // both bf16 (1) or both f16 (0) at bits 7-9 / 10-12, both K-major, N >> 3 at
 // bits 17-22, M >> 4 at bits 24-28.
-__host__ __device__ inline uint32_t qkv_idesc(bool bf16, int n) {
+__host__ __device__ inline uint32_t qkv_idesc(bool bf16, int m, int n) {
   const uint32_t f = bf16 ? 1u : 0u;
-  return (1u << 4) | (f << 7) | (f << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTileN >> 4) << 24);
+  return (1u << 4) | (f << 7) | (f << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -135,6 +139,12 @@ __device__ __forceinline__ T to_elem(float x);
 template <> __device__ __forceinline__ __nv_bfloat16 to_elem<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 template <> __device__ __forceinline__ __half to_elem<__half>(float x) { return __float2half_rn(x); }
 
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // First CTA whose unit range [g*U/G, (g+1)*U/G) contains unit x.
 __device__ __forceinline__ int first_cta(long long x, long long units, int grid) {
   return (int)(((x + 1) * grid - 1) / units);
@@ -153,29 +163,47 @@ __device__ __forceinline__ Segment segment_at(long long u, long long u_end, int 
   return s;
 }
 
+// Stream-K schedule for batches up to 128 (qkv_stream_kernel).  The weights
+// are the MMA's B operand: a tile is 256 output features (two packed
+// 128-feature chunks at the same K block, side by side in shared memory, so
+// one tcgen05.mma of N = 256, K = 16 consumes 8 KB of weights) against the
+// batch as M = 128 rows (x rows beyond the batch tile are never stored).
+// Every tcgen05.mma costs about the same issue time whatever its N, so
+// carrying the weights in N rather than M halves the instructions per
+// weight byte; with the weights in M (4 KB per instruction) the tensor pipe,
+// not HBM, set the streaming rate.
+//
+// The accumulator holds row b of the batch in tensor-memory lane b and
+// feature f in column f, so an epilogue thread owns one sequence and writes
+// 16 consecutive features (32 bytes) of its q row or cache slot per chunk.
 template <typename T>
 __global__ void __launch_bounds__(kQkvThreads, 1)
-    qkv_append_kernel(const __grid_constant__ CUtensorMap tm_x, const QkvArgs a) {
+    qkv_stream_kernel(const __grid_constant__ CUtensorMap tm_x, const QkvArgs a) {
   __shared__ __align__(8) uint64_t full_bar[16];
   __shared__ __align__(8) uint64_t empty_bar[16];
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int last_flag;
-  __shared__ int32_t slot_of[kMaxBatchTile];  // cache row of each batch column of the current tile (-1: skip)
+  __shared__ float inv_freq[kMaxHeadDim / 2];  // RoPE: theta^(-2i/D)
+  __shared__ float bias_s[kStreamN];             // the current tile's bias
+  __shared__ int row_pos[kStreamM], row_slot[kStreamM];  // per batch row: position, cache slot (-1: none)
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte aligned (the swizzle atom), by offsetting the shared array
   // itself so the compiler keeps the shared address space
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int BT = a.batch_tile;
-  const uint32_t a_bytes = kTileN * 128, b_bytes = (uint32_t)BT * 128;
-  const uint32_t stage_bytes = a_bytes + b_bytes;
-  T* stage_out = reinterpret_cast<T*>(smem + (size_t)a.nstage * stage_bytes);  // [BT][128] epilogue staging
+  const int BT = a.batch_tile;                        // x rows copied per stage (16..128)
+  constexpr uint32_t w_half = kTileN * 128;           // one packed 128-feature chunk: 16 KB
+  const uint32_t x_bytes = (uint32_t)BT * 128;
+  const uint32_t stage_bytes = 2 * w_half + x_bytes;  // weights [256][64], then x [BT][64]
   const int G = gridDim.x;
   const long long u_begin = (long long)blockIdx.x * a.units / G;
   const long long u_end = (long long)(blockIdx.x + 1) * a.units / G;
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0 && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 8 * blockIdx.x] = gtime();
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.nstage; ++s) {
@@ -188,10 +216,14 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
     }
     fence_barrier_init();
   }
+  if (a.rope_theta > 0.f)
+    for (int i = threadIdx.x; i < a.D / 2; i += blockDim.x)
+      inv_freq[i] = powf(a.rope_theta, -2.f * (float)i / (float)a.D);
   __syncwarp();
   if (warp == 0) {
+    // two accumulators of 256 columns: a segment drains while the next accumulates
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_slot)),
-                 "r"(2 * a.acc_cols)
+                 "r"(2 * kStreamN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -199,36 +231,53 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_slot;
+  // the next kernel on the stream may be scheduled now (it waits for this
+  // grid before reading anything)
+  griddep_launch_dependents();
 
   constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   if (warp == 0) {
     if (lane == 0) {
-      // producer: W^T tile [128 features, 64] and x tile [BT, 64] per stage
-      int i = 0;
-      bool ok = true;
+      // producer.  Stage i holds unit u_begin + i: tile u / kb_total, K
+      // block u % kb_total.  The packed weights are never written by the
+      // kernel this one may overlap (clove_cuda_qkv_pack_weights ends with a
+      // full dependency), so the first ring's worth of weight chunks is
+      // requested before griddepcontrol.wait; x, which the previous kernel
+      // may write, only after it.
       const bool stall = a.inject_stall && blockIdx.x == 0;
-      for (long long u = u_begin; u < u_end && ok;) {
-        const Segment sg = segment_at(u, u_end, a.kb_total);
-        u += sg.kb1 - sg.kb0;
-        const int m0 = (sg.tile / a.ntiles_n) * kMaxBatchTile;
-        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++i) {
-          const int s = i % a.nstage;
-          const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
-          if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1u, a.flags, a.wait_limit)) {
-            ok = false;
-            break;
-          }
-          if (stall && i == 0) continue;  // test hook: stage 0 never filled
-          unsigned char* st = smem + (size_t)s * stage_bytes;
-          mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
-          const int k0 = kb * kTileK;  // 64 elements = 128 bytes: meets the 16-byte rule
-          // the weight chunk of (feature tile, K block): 16 KB, contiguous and
-          // already in the swizzled order (clove_cuda_qkv_pack_weights)
-          bulk_load(st, static_cast<const unsigned char*>(a.w_packed) +
-                            ((size_t)(sg.tile % a.ntiles_n) * a.kb_total + kb) * a_bytes,
-                    a_bytes, &full_bar[s]);
-          tma_load_2d(st + a_bytes, &tm_x, &full_bar[s], k0, m0);
-        }
+      const int n = (int)(u_end - u_begin);
+      const int pre = min(n, a.nstage);
+      auto load_w = [&](int i) {
+        const long long u = u_begin + i;
+        const int tile = (int)(u / a.kb_total), kb = (int)(u % a.kb_total);
+        const int s = i % a.nstage;
+        unsigned char* st = smem + (size_t)s * stage_bytes;
+        // the second chunk is absent when the packed chunk count is odd: its
+        // features lie beyond n_out and are never stored
+        const bool two = 2 * tile + 1 < a.ntiles_n;
+        mbar_arrive_expect_tx(&full_bar[s], (two ? 2 : 1) * w_half + x_bytes);
+        const unsigned char* w = static_cast<const unsigned char*>(a.w_packed);
+        bulk_load(st, w + ((size_t)(2 * tile) * a.kb_total + kb) * w_half, w_half, &full_bar[s]);
+        if (two) bulk_load(st + w_half, w + ((size_t)(2 * tile + 1) * a.kb_total + kb) * w_half, w_half, &full_bar[s]);
+      };
+      auto load_x = [&](int i) {
+        const int k0 = (int)((u_begin + i) % a.kb_total) * kTileK;  // 64 elements = 128 bytes: the 16-byte rule
+        const int s = i % a.nstage;
+        tma_load_2d(smem + (size_t)s * stage_bytes + 2 * w_half, &tm_x, &full_bar[s], k0, 0);
+      };
+      for (int i = (stall ? 1 : 0); i < pre; ++i) load_w(i);  // fresh ring: no empty wait
+      griddep_wait();
+      if constexpr (kTrace) {
+        if (a.trace && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 8 * blockIdx.x + 1] = gtime();
+      }
+      for (int i = (stall ? 1 : 0); i < pre; ++i) load_x(i);  // test hook: stage 0 never filled
+      int i = pre;
+      for (; i < n; ++i) {
+        const int s = i % a.nstage;
+        const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
+        if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1u, a.flags, a.wait_limit)) break;
+        load_w(i);
+        load_x(i);
       }
       // drain: the last copies must land before the CTA exits
       for (int t = max(stall ? 1 : 0, i - a.nstage); t < i; ++t)
@@ -238,7 +287,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // MMA issuer: segment j accumulates in tensor-memory buffer j % 2
-      const uint32_t idesc = qkv_idesc(bf16, BT);
+      const uint32_t idesc = qkv_idesc(bf16, kStreamM, kStreamN);
       int i = 0, j = 0;
       bool ok = true;
       for (long long u = u_begin; u < u_end && ok; ++j) {
@@ -249,7 +298,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         // the epilogue has drained this buffer's previous segment
         ok = mbar_wait_bounded(&acc_empty[buf], (use & 1u) ^ 1u, a.flags, a.wait_limit);
         tc_fence_after();
-        const uint32_t d_tmem = tmem + (uint32_t)(buf * a.acc_cols);
+        const uint32_t d_tmem = tmem + (uint32_t)(buf * kStreamN);
         for (int kb = sg.kb0; kb < sg.kb1 && ok; ++kb, ++i) {
           const int s = i % a.nstage;
           const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
@@ -257,9 +306,15 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
             ok = false;
             break;
           }
+          if constexpr (kTrace) {
+            if (a.trace && i == 0 && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 8 * blockIdx.x + 2] = gtime();
+          }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + (size_t)s * stage_bytes);
-          const uint64_t da = sw128_kmajor_desc(sa), db = sw128_kmajor_desc(sa + a_bytes);
+          const uint32_t sw = smem_u32(smem + (size_t)s * stage_bytes);
+          // A = x rows (M 128; rows past the copied BT read the next stage's
+          // bytes and only feed accumulator rows that are never stored),
+          // B = the 256 weight rows
+          const uint64_t da = sw128_kmajor_desc(sw + 2 * w_half), db = sw128_kmajor_desc(sw);
 #pragma unroll
           for (int k = 0; k < kTileK / 16; ++k)  // 16 elements = 32 bytes = 2 descriptor units
             umma_f16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb > sg.kb0 || k > 0) ? 1u : 0u);
@@ -267,15 +322,73 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         }
         umma_commit(&acc_full[buf]);  // arrives once the segment's MMAs complete
       }
+      if constexpr (kTrace) {
+        if (a.trace && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 8 * blockIdx.x + 3] = gtime();
+      }
     }
     __syncwarp();
   } else {
-    // ---- epilogue warps 2-5.  Thread e owns output feature r of the tile
-    // (its tensor-memory lane: warp w reads lanes 32 (w % 4) ..).
+    // ---- epilogue warps 2-5.  They read context lengths, tables and the
+    // workspace, and write q and the cache: all after the previous kernel has
+    // finished.  Draining tensor memory, thread e owns batch row b (its
+    // tensor-memory lane: warp w reads lanes 32 (w % 4) ..).
+    griddep_wait();
     const int e = threadIdx.x - 64;
-    const int r = (warp & 3) * 32 + lane;
+    const int b = (warp & 3) * 32 + lane;
+    const bool live = b < a.M;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const int qd = a.hq * a.D, kd = a.hkv * a.D;
+    // per row: position and cache slot (-1: none), once per call
+    {
+      int slot = -1, pos = 0;
+      if (live) {
+        pos = __ldg(a.context_lens + b);
+        if (pos >= 0 && pos / a.bs < a.bt_stride) {
+          const int phys = __ldg(a.block_tables + (size_t)b * a.bt_stride + pos / a.bs);
+          if (phys >= 0 && phys < a.num_blocks) slot = phys * a.bs + pos % a.bs;
+          else if (blockIdx.x == 0) atomicOr(a.flags, CLOVE_FLAG_BLOCK_OOB);
+        } else if (blockIdx.x == 0) {
+          atomicOr(a.flags, CLOVE_FLAG_CTX_RANGE);
+        }
+        if (blockIdx.x == 0 && a.lens_out) a.lens_out[b] = pos + 1;
+      }
+      row_pos[b] = pos;
+      row_slot[b] = slot;
+    }
+    // bias, RoPE, round and store features [f0, f0 + 16) of row r (the q |
+    // k | v boundaries are multiples of 64 features: a chunk never straddles
+    // one); bias_s holds the current tile's bias
+    auto emit = [&](int r, int f0, int n0, float (&v)[16]) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] += bias_s[f0 - n0 + i];
+      if (a.rope_theta > 0.f && f0 < qd + kd) {
+        const int d0 = f0 % a.D;
+        const float pos = (float)row_pos[r];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          float sn, cs;
+          sincosf(pos * inv_freq[(d0 + i) >> 1], &sn, &cs);
+          const float x0 = v[i], x1 = v[i + 1];
+          v[i] = x0 * cs - x1 * sn;
+          v[i + 1] = x1 * cs + x0 * sn;
+        }
+      }
+      T* dst;
+      if (f0 < qd) {
+        dst = static_cast<T*>(a.q_out) + (size_t)r * qd + f0;
+      } else {
+        const int slot = row_slot[r];
+        if (slot < 0) return;
+        const bool is_k = f0 < qd + kd;
+        dst = static_cast<T*>(is_k ? a.k_cache : a.v_cache) + (size_t)slot * kd + (f0 - (is_k ? qd : qd + kd));
+      }
+      uint4 out[2];
+      T* o = reinterpret_cast<T*>(out);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = to_elem<T>(v[i]);
+      __stcs(reinterpret_cast<uint4*>(dst), out[0]);
+      __stcs(reinterpret_cast<uint4*>(dst) + 1, out[1]);
+    };
     int j = 0;
     bool aborted = false;
     for (long long u = u_begin; u < u_end; ++j) {
@@ -285,9 +398,17 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       const long long t0 = (long long)sg.tile * a.kb_total;
       const int g_first = first_cta(t0, a.units, G);
       const int n_contrib = first_cta(t0 + a.kb_total - 1, a.units, G) - g_first + 1;
+      const int n0 = sg.tile * kStreamN;
+      const int ncols = min(kStreamN, a.n_out - n0);  // a multiple of 64
+      // this tile's bias, once every thread is done with the previous one's
+      named_bar_sync(1, kEpiThreads);
+      for (int i = e; i < kStreamN; i += kEpiThreads) bias_s[i] = (a.bias && i < ncols) ? __ldg(a.bias + n0 + i) : 0.f;
       if (!aborted) {
         const bool ok = mbar_wait_bounded(&acc_full[(j & 1)], (uint32_t)(j >> 1) & 1u, a.flags, a.wait_limit);
         aborted = named_bar_or(1, kEpiThreads, !ok);  // every epilogue warp decides together
+      }
+      if constexpr (kTrace) {
+        if (a.trace && e == 0 && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 8 * blockIdx.x + 5] = gtime();
       }
       if (aborted) {
         // the flag is set; still count this CTA's pieces so that every tile's
@@ -295,139 +416,95 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
         if (!whole && e == 0 && atomicAdd(a.counters + sg.tile, 1) == n_contrib - 1) a.counters[sg.tile] = 0;
         continue;
       }
-      const int tile_n = sg.tile % a.ntiles_n, m0 = (sg.tile / a.ntiles_n) * kMaxBatchTile;
-      const int n0 = tile_n * kTileN;
-      const int f = n0 + r;
-      const float bias = (a.bias && f < a.n_out) ? __ldg(a.bias + f) : 0.f;
-      const int d = f % a.D;
-      // RoPE angle factor for this feature's pair (2i, 2i+1): theta^(-2i/D)
-      // (warp-uniform: a warp's 32 features never straddle a head boundary)
-      const bool rot = a.rope_theta > 0.f && f < qd + kd;
-      const float inv_freq = rot ? powf(a.rope_theta, -2.f * (float)(d >> 1) / (float)a.D) : 0.f;
-      auto finish = [&](int c, float val) -> T {  // c: column within the batch tile
-        val += bias;
-        if (rot) {
-          // partner element of the pair lives in the neighbouring lane
-          const float other = __shfl_xor_sync(0xffffffffu, val, 1);
-          const int b = m0 + c;
-          const int pos = b < a.M ? __ldg(a.context_lens + b) : 0;
-          float sn, cs;
-          sincosf((float)pos * inv_freq, &sn, &cs);
-          val = (d & 1) ? other * sn + val * cs : val * cs - other * sn;
-        }
-        return to_elem<T>(val);
-      };
-
       const int buf = j & 1;
       tc_fence_after();
-      // cache slot of each column, once per tile (read by the stores below,
-      // after the staging barrier)
-      for (int c = e; c < BT; c += kEpiThreads) {
-        const int b = m0 + c;
-        int slot = -1;
-        if (b < a.M) {
-          const int pos = __ldg(a.context_lens + b);
-          if (pos < 0 || pos / a.bs >= a.bt_stride) {
-            if (tile_n == 0) atomicOr(a.flags, CLOVE_FLAG_CTX_RANGE);
-          } else {
-            const int phys = __ldg(a.block_tables + (size_t)b * a.bt_stride + pos / a.bs);
-            if (phys >= 0 && phys < a.num_blocks) slot = phys * a.bs + pos % a.bs;
-            else if (tile_n == 0) atomicOr(a.flags, CLOVE_FLAG_BLOCK_OOB);
-          }
-          if (tile_n == 0 && a.lens_out) a.lens_out[b] = pos + 1;
-        }
-        slot_of[c] = slot;
-      }
-      const uint32_t acc = tmem + lane_off + (uint32_t)(buf * a.acc_cols);
+      const uint32_t acc = tmem + lane_off + (uint32_t)(buf * kStreamN);
       if (whole) {
-        // the whole tile in this CTA
-        for (int c0 = 0; c0 < BT; c0 += 16) {
+        for (int c0 = 0; c0 < ncols; c0 += 16) {
           float v[16];
           tmem_ld16(acc + (uint32_t)c0, v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) stage_out[(c0 + i) * kTileN + r] = finish(c0 + i, v[i]);
+          if (live) emit(b, n0 + c0, n0, v);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[buf]);
-      } else {
-        // a piece: publish the partial in this CTA's slot of the tile
-        float* part = a.partials + (size_t)sg.tile * a.max_contrib * BT * kTileN;
-        float* mine = part + (size_t)(blockIdx.x - g_first) * BT * kTileN;
-        // feature-major [slot][feature][column]: each thread moves its own
-        // columns with 16-byte accesses
-        float* my_row = mine + (size_t)r * BT;
-        for (int c0 = 0; c0 < BT; c0 += 16) {
+        continue;
+      }
+      // A piece: publish its partial.  Partials are float4s laid out
+      // [slot][16-feature chunk][quarter][row], so the 32 lanes of a warp (32
+      // consecutive rows) move 512 contiguous bytes per access.
+      const size_t slot_stride = (size_t)(kStreamN / 16) * 4 * BT;  // float4s per slot
+      float4* part4 = reinterpret_cast<float4*>(a.partials) + (size_t)sg.tile * a.max_contrib * slot_stride;
+      {
+        float4* mine = part4 + (size_t)(blockIdx.x - g_first) * slot_stride + b;
+        for (int c0 = 0; c0 < ncols; c0 += 16) {
           float v[16];
           tmem_ld16(acc + (uint32_t)c0, v);
+          if (live) {
 #pragma unroll
-          for (int i = 0; i < 16; i += 4)
-            __stcg(reinterpret_cast<float4*>(my_row + c0 + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
-        }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[buf]);
-        __threadfence();  // the partial is visible before this CTA's arrival is counted
-        named_bar_sync(1, kEpiThreads);
-        if (e == 0) last_flag = atomicAdd(a.counters + sg.tile, 1) == n_contrib - 1;
-        named_bar_sync(1, kEpiThreads);
-        if (!last_flag) continue;
-        // last piece of the tile: sum the partials in slot order
-        __threadfence();
-        if (e == 0) a.counters[sg.tile] = 0;  // zero again for the next call
-        for (int c0 = 0; c0 < BT; c0 += 16) {
-          float sum[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) sum[i] = 0.f;
-#pragma unroll 2
-          for (int p = 0; p < n_contrib; ++p) {
-            const float4* src = reinterpret_cast<const float4*>(part + ((size_t)p * kTileN + r) * BT + c0);
-            float4 t[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) t[i] = __ldcg(src + i);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              sum[4 * i] += t[i].x;
-              sum[4 * i + 1] += t[i].y;
-              sum[4 * i + 2] += t[i].z;
-              sum[4 * i + 3] += t[i].w;
-            }
+            for (int i = 0; i < 4; ++i)
+              __stcg(mine + (size_t)(c0 / 16 * 4 + i) * BT, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
           }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+      __threadfence();  // the partial is visible before this CTA's arrival is counted
+      named_bar_sync(1, kEpiThreads);
+      if (e == 0) last_flag = atomicAdd(a.counters + sg.tile, 1) == n_contrib - 1;
+      named_bar_sync(1, kEpiThreads);
+      if (!last_flag) continue;
+      // the tile's last piece: sum the slots in order and run the epilogue,
+      // spread over (row, chunk) items with the row fastest (coalesced
+      // loads), up to eight slots' loads in flight per item
+      __threadfence();
+      if (e == 0) a.counters[sg.tile] = 0;  // zero again for the next call
+      if constexpr (kTrace) {
+        if (a.trace && e == 0 && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 8 * blockIdx.x + 6] = gtime();
+      }
+      const int M = min(a.M, BT);
+      const int items = M * (ncols / 16);
+      for (int it = e; it < items; it += kEpiThreads) {
+        const int r = it % M, c = it / M;
+        const float4* src = part4 + (size_t)c * 4 * BT + r;
+        float sum[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) stage_out[(c0 + i) * kTileN + r] = finish(c0 + i, sum[i]);
+        for (int i = 0; i < 16; ++i) sum[i] = 0.f;
+        for (int p0 = 0; p0 < n_contrib; p0 += 8) {
+          float4 t[8][4];
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (p0 + q < n_contrib) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) t[q][i] = __ldcg(src + (size_t)(p0 + q) * slot_stride + (size_t)i * BT);
+            }
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (p0 + q < n_contrib) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                sum[4 * i] += t[q][i].x;
+                sum[4 * i + 1] += t[q][i].y;
+                sum[4 * i + 2] += t[q][i].z;
+                sum[4 * i + 3] += t[q][i].w;
+              }
+            }
         }
+        emit(r, n0 + c * 16, n0, sum);
       }
-      named_bar_sync(1, kEpiThreads);  // staging complete
-      // 16-byte stores: 16 chunks of 8 features per column.  Section
-      // boundaries (q | k | v) are multiples of 64 features, so a chunk never
-      // straddles one.
-      for (int q = e; q < BT * 16; q += kEpiThreads) {
-        const int c = q >> 4, f0 = n0 + (q & 15) * 8;
-        const int b = m0 + c;
-        if (b >= a.M || f0 >= a.n_out) continue;
-        const uint4 val = *reinterpret_cast<const uint4*>(stage_out + (size_t)c * kTileN + (q & 15) * 8);
-        T* dst;
-        if (f0 < qd) {
-          dst = static_cast<T*>(a.q_out) + (size_t)b * qd + f0;
-        } else {
-          const int slot = slot_of[c];
-          if (slot < 0) continue;
-          const bool is_k = f0 < qd + kd;
-          dst = static_cast<T*>(is_k ? a.k_cache : a.v_cache) + (size_t)slot * kd + (f0 - (is_k ? qd : qd + kd));
-        }
-        __stcs(reinterpret_cast<uint4*>(dst), val);
-      }
-      named_bar_sync(1, kEpiThreads);  // staging free for the next tile
+    }
+    if constexpr (kTrace) {
+      if (a.trace && e == 0 && blockIdx.x < kTraceMaxCta) a.trace[kTraceCta + 8 * blockIdx.x + 4] = gtime();
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * a.acc_cols)
-                 : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kStreamN) : "memory");
   }
 }
 
-// Cluster schedule for batch tiles above 32 columns: grid (feature tiles) x
+// Cluster schedule for batches above 128: grid (feature tiles) x
 // (K splits) x (batch tiles), the K splits of a feature tile forming one
 // thread-block cluster.  Each CTA accumulates its K range in tensor memory;
 // the CTAs then push each other's columns through distributed shared memory
@@ -479,28 +556,39 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_slot;
+  // the next kernel on the stream may be scheduled now (it waits for this
+  // grid before reading anything)
+  griddep_launch_dependents();
 
   constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   if (warp == 0) {
     if (lane == 0) {
-      // producer: W^T tile [128 features, 64] and x tile [BT, 64] per stage
-      int issued = 0;
+      // producer: W^T tile [128 features, 64] and x tile [BT, 64] per stage;
+      // the first ring's worth of weight chunks before griddepcontrol.wait
+      // (the packed weights are never written by the kernel this one may
+      // overlap), x only after it
       const bool stall = a.inject_stall && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % a.nstage;
-        const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
-        if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1u, a.flags, a.wait_limit)) break;
-        if (stall && i == 0) {  // test hook: stage 0 never filled
-          ++issued;
-          continue;
-        }
-        unsigned char* st = smem + (size_t)s * stage_bytes;
-        mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
-        const int k0 = (kb0 + i) * kTileK;  // 64 elements = 128 bytes: meets the 16-byte rule
+      const int pre = min(nkb, a.nstage);
+      auto load_w = [&](int i) {
+        unsigned char* st = smem + (size_t)(i % a.nstage) * stage_bytes;
+        mbar_arrive_expect_tx(&full_bar[i % a.nstage], stage_bytes);
         // the weight chunk of (feature tile, K block): 16 KB, contiguous, pre-swizzled
         bulk_load(st, static_cast<const unsigned char*>(a.w_packed) + ((size_t)tile_n * a.kb_total + kb0 + i) * a_bytes,
-                  a_bytes, &full_bar[s]);
-        tma_load_2d(st + a_bytes, &tm_x, &full_bar[s], k0, m0);
+                  a_bytes, &full_bar[i % a.nstage]);
+      };
+      auto load_x = [&](int i) {
+        const int k0 = (kb0 + i) * kTileK;  // 64 elements = 128 bytes: meets the 16-byte rule
+        tma_load_2d(smem + (size_t)(i % a.nstage) * stage_bytes + a_bytes, &tm_x, &full_bar[i % a.nstage], k0, m0);
+      };
+      for (int i = (stall ? 1 : 0); i < pre; ++i) load_w(i);  // fresh ring: no empty wait
+      griddep_wait();
+      for (int i = (stall ? 1 : 0); i < pre; ++i) load_x(i);  // test hook: stage 0 never filled
+      int issued = pre;
+      for (int i = pre; i < nkb; ++i) {
+        const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
+        if (!mbar_wait_bounded(&empty_bar[i % a.nstage], ph ^ 1u, a.flags, a.wait_limit)) break;
+        load_w(i);
+        load_x(i);
         ++issued;
       }
       // drain: the copies issued last must have landed before shared memory is reused
@@ -511,7 +599,7 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // MMA issuer
-      const uint32_t idesc = qkv_idesc(bf16, BT);
+      const uint32_t idesc = qkv_idesc(bf16, kTileN, BT);
       for (int i = 0; i < nkb; ++i) {
         const int s = i % a.nstage;
         const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
@@ -528,8 +616,9 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
     }
     __syncwarp();
   } else {
-    // warps 2-3, idle during the main loop: the cache slot of each batch
+    // warps 2-7, idle during the main loop: the cache slot of each batch
     // column from its sequence's block table (read after the barrier below)
+    griddep_wait();
     for (int c = threadIdx.x - 64; c < BT; c += kClusterThreads - 64) {  // warps 2-7
       const int b = m0 + c;
       int slot = -1;
@@ -547,6 +636,8 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
       slot_of[c] = slot;
     }
   }
+
+  griddep_wait();  // warps 0-1 (the others have waited already): bias, context lengths, outputs
 
   // ---- epilogue.  Thread t computes feature r = t % 128 (its tensor-memory
   // lane) for the columns of its half h = t / 128 (alternating 16-column
@@ -709,6 +800,8 @@ static int encode_operand_map(CUtensorMap* map, const void* base, int dtype, int
 // kb, row r, position p) holds the 8 elements of W^T row t*128 + r, columns
 // kb*64 + 8 (p ^ (r % 8)) .. +7 — the 128-byte swizzle that the bulk-tensor
 // copies would apply — with zeros past n_out / hidden.
+__global__ void stream_fence_kernel() {}
+
 template <typename T>
 __global__ void pack_weights_kernel(const T* __restrict__ w_t, T* __restrict__ out, int n_out, int hidden,
                                     int kb_total, long long chunks) {
@@ -736,39 +829,56 @@ static size_t packed_bytes(int n_out, int hidden) {
 // Schedule and workspace of one call.
 struct QkvPlan {
   bool stream_k;  // false: the cluster schedule
-  int batch_tile, ntiles_n, n_btiles, kb_total, grid, max_contrib, nstage, acc_cols;
+  int batch_tile, ntiles_n, n_btiles, kb_total, grid, max_contrib, nstage;
   long long units;
   size_t smem, off_partials, ws_bytes;
 };
 
+// Stage-ring bytes per CTA: the built-in budget, or CLOVE_QKV_RING_KB (a
+// tuning override, read once) when that is smaller.
+static size_t ring_budget(size_t builtin) {
+  static const size_t env = [] {
+    const char* v = std::getenv("CLOVE_QKV_RING_KB");
+    return v ? (size_t)std::max(0L, std::atol(v)) * 1024 : (size_t)0;
+  }();
+  return env ? std::min(env, builtin) : builtin;
+}
+
 static QkvPlan plan_qkv(const clove_pool& pool, int batch, int hidden, int num_q_heads) {
   QkvPlan P;
-  P.n_btiles = (batch + kMaxBatchTile - 1) / kMaxBatchTile;
-  P.batch_tile = P.n_btiles > 1 ? kMaxBatchTile : ((batch + 15) / 16) * 16;
   const int n_out = (num_q_heads + 2 * pool.num_kv_heads) * pool.head_dim;
   P.ntiles_n = (n_out + kTileN - 1) / kTileN;
   P.kb_total = (hidden + kTileK - 1) / kTileK;
-  P.units = (long long)P.ntiles_n * P.n_btiles * P.kb_total;
-  // Stream-K for small batch tiles (partials are cheap to sum), and for
-  // tiles up to 64 columns when the cluster grid (feature tiles x K splits)
-  // would leave over 40 % of the SMs idle; clusters otherwise.
-  const int tiles_mn = P.ntiles_n * P.n_btiles;
-  const int splits_hint = std::max(1, std::min({pool.num_sms / tiles_mn, 8, std::max(1, P.kb_total / 2)}));
-  P.stream_k = P.batch_tile <= kStreamKMaxTile ||
-               (P.batch_tile <= 2 * kStreamKMaxTile && 10 * tiles_mn * splits_hint < 6 * pool.num_sms);
-  // one CTA per SM, at least two K blocks each
-  P.grid = (int)std::max(1LL, std::min((long long)pool.num_sms, P.units / 2));
-  const long long per_cta = P.units / P.grid;  // shortest range
-  P.max_contrib = (int)std::min((long long)P.grid, (P.kb_total + per_cta - 1) / per_cta + 1);
-  P.acc_cols = P.batch_tile <= 32 ? 32 : P.batch_tile <= 64 ? 64 : P.batch_tile <= 128 ? 128 : 256;
-  const size_t stage = (size_t)kTileN * 128 + (size_t)P.batch_tile * 128;
-  const size_t staging = (size_t)P.batch_tile * kTileN * 2;
-  P.nstage = (int)std::min<size_t>(16, (kSmemBudget - staging) / stage);
-  P.smem = stage * P.nstage + staging + 1024;
-  const size_t tiles = (size_t)P.ntiles_n * P.n_btiles;
-  P.off_partials = (tiles * 4 + 255) & ~size_t(255);
-  P.ws_bytes = P.stream_k ? P.off_partials + tiles * P.max_contrib * P.batch_tile * kTileN * 4
-                                                : 256;  // the cluster schedule needs no workspace
+  P.stream_k = batch <= kStreamMaxBatch;
+  if (P.stream_k) {
+    // (256-feature tile) x (64-wide K block) units, split evenly and
+    // contiguously over one CTA per SM, at least two K blocks each
+    P.n_btiles = 1;
+    P.batch_tile = ((batch + 15) / 16) * 16;
+    const long long tiles = (P.ntiles_n + 1) / 2;
+    P.units = tiles * P.kb_total;
+    P.grid = (int)std::max(1LL, std::min((long long)pool.num_sms, P.units / 2));
+    const long long per_cta = P.units / P.grid;  // shortest range
+    P.max_contrib = (int)std::min((long long)P.grid, (P.kb_total + per_cta - 1) / per_cta + 1);
+    // stage: two weight chunks + x [batch_tile][64]; the MMA reads 128 x
+    // rows, so the last stage is followed by padding up to 128 rows
+    const size_t stage = 2 * (size_t)kTileN * 128 + (size_t)P.batch_tile * 128;
+    const size_t pad = (size_t)(kStreamM - P.batch_tile) * 128;
+    P.nstage = (int)std::max<size_t>(2, std::min<size_t>(16, ring_budget(kSmemBudget - pad) / stage));
+    P.smem = stage * P.nstage + pad + 1024;
+    P.off_partials = ((size_t)tiles * 4 + 255) & ~size_t(255);
+    P.ws_bytes = P.off_partials + (size_t)tiles * P.max_contrib * P.batch_tile * kStreamN * 4;
+  } else {
+    P.n_btiles = (batch + kMaxBatchTile - 1) / kMaxBatchTile;
+    P.batch_tile = P.n_btiles > 1 ? kMaxBatchTile : ((batch + 15) / 16) * 16;
+    P.units = (long long)P.ntiles_n * P.n_btiles * P.kb_total;
+    P.grid = 0;  // chosen at launch (cluster occupancy)
+    P.max_contrib = 0;
+    P.nstage = 0;
+    P.smem = 0;
+    P.off_partials = 0;
+    P.ws_bytes = 256;  // the cluster schedule needs no workspace
+  }
   return P;
 }
 
@@ -796,12 +906,17 @@ int clove_cuda_qkv_pack_weights(int dtype, const void* w_t, int n_out, int hidde
   else
     pack_weights_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(w_t), static_cast<__half*>(packed),
                                                        n_out, hidden, kb_total, chunks);
+  // An empty kernel with an ordinary (full) dependency on the packing: the
+  // projection kernel, a programmatic dependent of whatever precedes it,
+  // reads weights before its griddepcontrol.wait, so the kernel right before
+  // it must not be the one that wrote them.
+  stream_fence_kernel<<<1, 32, 0, s>>>();
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_last_error("qkv_pack_weights launch: %s", cudaGetErrorString(e));
     return CLOVE_ERR_CUDA;
   }
-  count_launches(1);
+  count_launches(2);
   return CLOVE_OK;
 }
 
@@ -865,10 +980,10 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x, const void* w_packed
   a.batch_tile = P.batch_tile;
   a.nstage = P.nstage;
   a.max_contrib = P.max_contrib;
-  a.acc_cols = P.acc_cols;
   a.units = P.units;
   a.rope_theta = rope_theta;
   a.inject_stall = debug_inject_stall();
+  a.trace = kTrace ? trace_buffer() : nullptr;
   const uint32_t lim = debug_wait_limit();
   a.wait_limit = lim ? lim : kWaitLimit;
 
@@ -882,25 +997,39 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x, const void* w_packed
   if (prev != pool->device) cudaSetDevice(pool->device);
   cudaError_t e = cudaSuccess;
   if (P.stream_k) {
-    auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_append_kernel<__nv_bfloat16> : qkv_append_kernel<__half>;
+    auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_stream_kernel<__nv_bfloat16> : qkv_stream_kernel<__half>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem);
-    if (e == cudaSuccess)
-      kern<<<P.grid, kQkvThreads, P.smem, static_cast<cudaStream_t>(stream)>>>(tm_x, a);
-    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e == cudaSuccess) {
+      // a programmatic dependent of the previous kernel on the stream: its
+      // set-up and first weight copies overlap that kernel's tail
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(P.grid);
+      cfg.blockDim = dim3(kQkvThreads);
+      cfg.dynamicSmemBytes = P.smem;
+      cfg.stream = static_cast<cudaStream_t>(stream);
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      e = cudaLaunchKernelEx(&cfg, kern, tm_x, a);
+    }
   } else {
     auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_cluster_kernel<__nv_bfloat16> : qkv_cluster_kernel<__half>;
     const int ntiles = P.ntiles_n;
     const size_t stage = (size_t)kTileN * 128 + (size_t)P.batch_tile * 128;
-    a.nstage = (int)std::min<size_t>(16, kRingBudget / stage);
+    a.nstage = (int)std::max<size_t>(2, std::min<size_t>(16, ring_budget(kRingBudget) / stage));
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(kClusterThreads);
     cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // as above
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 1;  // the occupancy query below sees the cluster shape only
     // K splits: enough CTAs to cover the SMs, at most 8 (portable cluster),
     // at least 2 K blocks each, and few enough clusters to be resident at
     // once (a second wave would double the time)
@@ -926,6 +1055,7 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x, const void* w_packed
       cfg.gridDim = dim3(ntiles, splits, P.n_btiles);
       cfg.dynamicSmemBytes = smem;
       attr[0].val.clusterDim.y = splits;
+      cfg.numAttrs = 2;
       e = cudaLaunchKernelEx(&cfg, kern, tm_x, a);
     }
   }

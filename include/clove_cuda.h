@@ -213,8 +213,9 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k,
  * and stores k, v at slot context_lens[b] of sequence b through
  * block_tables.  With rope_theta > 0, q and k are rotated by position
  * context_lens[b] (the pairing of clove_cuda_paged_prefill).
- * context_lens_out (optional, int32 [batch]) receives context_lens + 1: the
- * lengths to decode over with clove_cuda_paged_decode.  Bad slots are
+ * context_lens_out (optional, int32 [batch], not aliasing context_lens)
+ * receives context_lens + 1: the lengths to decode over with
+ * clove_cuda_paged_decode.  Bad slots are
  * skipped and flagged in the pool's status word, like
  * clove_cuda_reshape_and_cache.  Scratch: clove_cuda_qkv_workspace_size
  * bytes, 256-byte aligned, ZERO-FILLED before its first use; every call

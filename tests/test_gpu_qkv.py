@@ -51,7 +51,7 @@ def _run(dtype, B, hidden, hq, hkv, D, bs, theta, with_bias=True, seed=0):
     assert pool.pool_status() == 0
     assert np.array_equal(lens.cpu().numpy(), ctx + 1)
     # the per-tile arrival counters at the workspace's start are zero again
-    tiles = -(-n_out // 128) * -(-B // 256)
+    tiles = -(-n_out // 256) if B <= 128 else 0  # stream-K: one counter per 256-feature tile
     assert int(pool._qkv_ws[:4 * tiles].view(torch.int32).abs().sum()) == 0
     # oracle: W [hidden, out] per projection as the reference stores it
     wf = w.double().cpu().numpy()
@@ -89,7 +89,9 @@ def _run(dtype, B, hidden, hq, hkv, D, bs, theta, with_bias=True, seed=0):
     (33, 520, 4, 4, 64, 8, 10000.0),       # hidden not a multiple of 64 (zero-filled tail)
     (64, 8192, 64, 8, 128, 16, 0.0),       # 70B-shaped projection
     (7, 384, 3, 1, 64, 16, 10000.0),       # 320 features: a partial last tile, q/k boundary mid-tile
-    (40, 384, 3, 1, 64, 16, 10000.0),      # the same through the cluster schedule
+    (140, 384, 3, 1, 64, 16, 10000.0),     # the same through the cluster schedule
+    (1, 4096, 32, 8, 128, 16, 10000.0),    # batch 1: one live row of the 128-row tile
+    (100, 2048, 16, 8, 128, 16, 0.0),      # ragged batch tile of 112 rows
 ])
 def test_qkv_append_matches_oracle(dtype, B, hidden, hq, hkv, D, bs, theta):
     _run(dtype, B, hidden, hq, hkv, D, bs, theta, seed=B + hidden)
@@ -99,7 +101,7 @@ def test_qkv_append_without_bias():
     _run(torch.bfloat16, 16, 256, 4, 2, 128, 16, 0.0, with_bias=False, seed=3)
 
 
-@pytest.mark.parametrize("pad", [0, 38])  # batch 2 (stream-K schedule) and 40 (cluster schedule)
+@pytest.mark.parametrize("pad", [0, 138])  # batch 2 (stream-K schedule) and 140 (cluster schedule)
 def test_qkv_append_flags_bad_slots_and_rejects_f32(pad):
     from clove_b200 import KVPool, _lib
     dev = torch.device("cuda", 0)
@@ -110,7 +112,7 @@ def test_qkv_append_flags_bad_slots_and_rejects_f32(pad):
     x = torch.randn((B, 128), device=dev).to(torch.bfloat16)
     w = torch.randn((n_out, 128), device=dev).to(torch.bfloat16)
     # seq 0: position past its table; seq 1: block id out of range; the rest valid
-    bt = torch.tensor([[0, 1], [99, 2]] + [[8 + i, 0] for i in range(pad)], dtype=torch.int32, device=dev)
+    bt = torch.tensor([[0, 1], [9999, 2]] + [[8 + i, 0] for i in range(pad)], dtype=torch.int32, device=dev)
     ctx = torch.tensor([40, 3] + [5] * pad, dtype=torch.int32, device=dev)
     pool.qkv_append(x, pool.pack_qkv_weights(w), None, 4, bt, ctx)
     torch.cuda.synchronize()
@@ -161,7 +163,7 @@ def test_fused_module_forward_matches_unfused(theta):
     assert ok, worst
 
 
-@pytest.mark.parametrize("B", [5, 128])  # stream-K and cluster schedules
+@pytest.mark.parametrize("B", [5, 160])  # stream-K and cluster schedules
 def test_stuck_wait_times_out_and_next_call_is_correct(B):
     # Failure detection without a GPU fault: the test hook leaves the first
     # stage of the first CTA unfilled, so the bounded waits run out; the call
@@ -191,7 +193,7 @@ def test_stuck_wait_times_out_and_next_call_is_correct(B):
         L.clove_cuda_debug_set(0, 0)
     assert flags & _lib.FLAG_TIMEOUT, flags
     assert elapsed < 30
-    tiles = -(-n_out // 128)
+    tiles = -(-n_out // 256) if B <= 128 else 0
     assert int(pool._qkv_ws[:4 * tiles].view(torch.int32).abs().sum()) == 0
     q, _ = pool.qkv_append(x, wp, None, hq, bt, ctx)
     torch.cuda.synchronize()
