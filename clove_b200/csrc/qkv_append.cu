@@ -52,6 +52,7 @@
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <string>
 #include <tuple>
 #include <type_traits>
 
@@ -163,6 +164,85 @@ __device__ __forceinline__ Segment segment_at(long long u, long long u_end, int 
   return s;
 }
 
+// Epilogue state of the kernels that carry the weights in N: RoPE factors,
+// the current tile's bias, and each batch row's position and cache slot.
+struct RowState {
+  float inv_freq[kMaxHeadDim / 2];  // RoPE: theta^(-2i/D)
+  float bias[kStreamN];             // the current 256-feature tile's bias
+  int pos[kStreamM];                // context length of each batch row
+  int slot[kStreamM];               // its cache slot (-1: none)
+};
+
+// Threads tid = 0, stride, 2 stride .. fill the RoPE factors and the
+// positions and slots of batch rows m0 .. m0 + batch_tile - 1 (rs index r =
+// row - m0); `report` (one CTA per batch tile) also flags bad positions /
+// blocks and writes the new lengths.  Reads context lengths and
+// tables: call after griddepcontrol.wait.
+__device__ __forceinline__ void init_rows(const QkvArgs& a, RowState& rs, int m0, int tid, int stride, bool report) {
+  if (a.rope_theta > 0.f)
+    for (int i = tid; i < a.D / 2; i += stride) rs.inv_freq[i] = powf(a.rope_theta, -2.f * (float)i / (float)a.D);
+  for (int r = tid; r < a.batch_tile; r += stride) {
+    const int b = m0 + r;
+    int slot = -1, pos = 0;
+    if (b < a.M) {
+      pos = __ldg(a.context_lens + b);
+      if (pos >= 0 && pos / a.bs < a.bt_stride) {
+        const int phys = __ldg(a.block_tables + (size_t)b * a.bt_stride + pos / a.bs);
+        if (phys >= 0 && phys < a.num_blocks) slot = phys * a.bs + pos % a.bs;
+        else if (report) atomicOr(a.flags, CLOVE_FLAG_BLOCK_OOB);
+      } else if (report) {
+        atomicOr(a.flags, CLOVE_FLAG_CTX_RANGE);
+      }
+      if (report && a.lens_out) a.lens_out[b] = pos + 1;
+    }
+    rs.pos[r] = pos;
+    rs.slot[r] = slot;
+  }
+}
+
+// Bias, RoPE, round and store features [f0, f0 + 16) of batch row m0 + r
+// (n0: the tile's first feature, whose bias rs.bias holds).  The q | k | v
+// boundaries are multiples of 64 features, so a chunk never straddles one.
+template <typename T>
+__device__ __forceinline__ void emit_chunk(const QkvArgs& a, const RowState& rs, int m0, int r, int f0, int n0,
+                                           float (&v)[16]) {
+  const int qd = a.hq * a.D, kd = a.hkv * a.D;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] += rs.bias[f0 - n0 + i];
+  if (a.rope_theta > 0.f && f0 < qd + kd) {
+    const int d0 = f0 % a.D;
+    const float pos = (float)rs.pos[r];
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      float sn, cs;
+      sincosf(pos * rs.inv_freq[(d0 + i) >> 1], &sn, &cs);
+      const float x0 = v[i], x1 = v[i + 1];
+      v[i] = x0 * cs - x1 * sn;
+      v[i + 1] = x1 * cs + x0 * sn;
+    }
+  }
+  T* dst;
+  if (f0 < qd) {
+    dst = static_cast<T*>(a.q_out) + (size_t)(m0 + r) * qd + f0;
+  } else {
+    const int slot = rs.slot[r];
+    if (slot < 0) return;
+    const bool is_k = f0 < qd + kd;
+    dst = static_cast<T*>(is_k ? a.k_cache : a.v_cache) + (size_t)slot * kd + (f0 - (is_k ? qd : qd + kd));
+  }
+  uint4 out[2];
+  T* o = reinterpret_cast<T*>(out);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i] = to_elem<T>(v[i]);
+  __stcs(reinterpret_cast<uint4*>(dst), out[0]);
+  __stcs(reinterpret_cast<uint4*>(dst) + 1, out[1]);
+}
+
+// Load the bias of features [n0, n0 + 256) into rs.bias (zeros past ncols).
+__device__ __forceinline__ void load_tile_bias(const QkvArgs& a, RowState& rs, int n0, int ncols, int tid, int stride) {
+  for (int i = tid; i < kStreamN; i += stride) rs.bias[i] = (a.bias && i < ncols) ? __ldg(a.bias + n0 + i) : 0.f;
+}
+
 // Stream-K schedule for batches up to 128 (qkv_stream_kernel).  The weights
 // are the MMA's B operand: a tile is 256 output features (two packed
 // 128-feature chunks at the same K block, side by side in shared memory, so
@@ -185,9 +265,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int last_flag;
-  __shared__ float inv_freq[kMaxHeadDim / 2];  // RoPE: theta^(-2i/D)
-  __shared__ float bias_s[kStreamN];             // the current tile's bias
-  __shared__ int row_pos[kStreamM], row_slot[kStreamM];  // per batch row: position, cache slot (-1: none)
+  __shared__ RowState rs;
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte aligned (the swizzle atom), by offsetting the shared array
   // itself so the compiler keeps the shared address space
@@ -216,9 +294,6 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
     }
     fence_barrier_init();
   }
-  if (a.rope_theta > 0.f)
-    for (int i = threadIdx.x; i < a.D / 2; i += blockDim.x)
-      inv_freq[i] = powf(a.rope_theta, -2.f * (float)i / (float)a.D);
   __syncwarp();
   if (warp == 0) {
     // two accumulators of 256 columns: a segment drains while the next accumulates
@@ -337,58 +412,8 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
     const int b = (warp & 3) * 32 + lane;
     const bool live = b < a.M;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const int qd = a.hq * a.D, kd = a.hkv * a.D;
-    // per row: position and cache slot (-1: none), once per call
-    {
-      int slot = -1, pos = 0;
-      if (live) {
-        pos = __ldg(a.context_lens + b);
-        if (pos >= 0 && pos / a.bs < a.bt_stride) {
-          const int phys = __ldg(a.block_tables + (size_t)b * a.bt_stride + pos / a.bs);
-          if (phys >= 0 && phys < a.num_blocks) slot = phys * a.bs + pos % a.bs;
-          else if (blockIdx.x == 0) atomicOr(a.flags, CLOVE_FLAG_BLOCK_OOB);
-        } else if (blockIdx.x == 0) {
-          atomicOr(a.flags, CLOVE_FLAG_CTX_RANGE);
-        }
-        if (blockIdx.x == 0 && a.lens_out) a.lens_out[b] = pos + 1;
-      }
-      row_pos[b] = pos;
-      row_slot[b] = slot;
-    }
-    // bias, RoPE, round and store features [f0, f0 + 16) of row r (the q |
-    // k | v boundaries are multiples of 64 features: a chunk never straddles
-    // one); bias_s holds the current tile's bias
-    auto emit = [&](int r, int f0, int n0, float (&v)[16]) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] += bias_s[f0 - n0 + i];
-      if (a.rope_theta > 0.f && f0 < qd + kd) {
-        const int d0 = f0 % a.D;
-        const float pos = (float)row_pos[r];
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          float sn, cs;
-          sincosf(pos * inv_freq[(d0 + i) >> 1], &sn, &cs);
-          const float x0 = v[i], x1 = v[i + 1];
-          v[i] = x0 * cs - x1 * sn;
-          v[i + 1] = x1 * cs + x0 * sn;
-        }
-      }
-      T* dst;
-      if (f0 < qd) {
-        dst = static_cast<T*>(a.q_out) + (size_t)r * qd + f0;
-      } else {
-        const int slot = row_slot[r];
-        if (slot < 0) return;
-        const bool is_k = f0 < qd + kd;
-        dst = static_cast<T*>(is_k ? a.k_cache : a.v_cache) + (size_t)slot * kd + (f0 - (is_k ? qd : qd + kd));
-      }
-      uint4 out[2];
-      T* o = reinterpret_cast<T*>(out);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) o[i] = to_elem<T>(v[i]);
-      __stcs(reinterpret_cast<uint4*>(dst), out[0]);
-      __stcs(reinterpret_cast<uint4*>(dst) + 1, out[1]);
-    };
+    init_rows(a, rs, 0, e, kEpiThreads, blockIdx.x == 0);  // visible after the first barrier below
+    auto emit = [&](int r, int f0, int n0, float (&v)[16]) { emit_chunk<T>(a, rs, 0, r, f0, n0, v); };
     int j = 0;
     bool aborted = false;
     for (long long u = u_begin; u < u_end; ++j) {
@@ -402,7 +427,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       const int ncols = min(kStreamN, a.n_out - n0);  // a multiple of 64
       // this tile's bias, once every thread is done with the previous one's
       named_bar_sync(1, kEpiThreads);
-      for (int i = e; i < kStreamN; i += kEpiThreads) bias_s[i] = (a.bias && i < ncols) ? __ldg(a.bias + n0 + i) : 0.f;
+      load_tile_bias(a, rs, n0, ncols, e, kEpiThreads);
       if (!aborted) {
         const bool ok = mbar_wait_bounded(&acc_full[(j & 1)], (uint32_t)(j >> 1) & 1u, a.flags, a.wait_limit);
         aborted = named_bar_or(1, kEpiThreads, !ok);  // every epilogue warp decides together
@@ -501,6 +526,223 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kStreamN) : "memory");
+  }
+}
+
+// Cluster schedule with the weights in N (qkv_cluster_n_kernel), when the
+// 256-feature tiles times the 128-row batch tiles times a cluster's K splits
+// cover the SMs: grid (feature tiles) x (splits) x (batch tiles), the splits
+// of a tile forming one thread-block cluster, each CTA accumulating its K range as in the
+// stream-K kernel (M = 128 batch rows, N = 256 features, one accumulator).
+// The split-K reduction runs through distributed shared memory: CTA j of the
+// cluster owns batch rows [j rs, (j + 1) rs); after the main loops every CTA
+// pushes its sums of each owner's rows into that owner's receive buffer
+// (overlaying the now idle stage ring), and each owner adds the S partial
+// sums in rank order and runs the epilogue for its rows — no global
+// workspace, no atomics, and the reduction spread over the cluster.
+// 256 threads: warp 0 copies, warp 1 MMAs, warps 2-7 look up the rows; all 8
+// drain tensor memory (warp w: lanes 32 (w % 4) .., alternating 16-column
+// chunks by w / 4) and run the epilogue.
+template <typename T>
+__global__ void __launch_bounds__(kClusterThreads, 1)
+    qkv_cluster_n_kernel(const __grid_constant__ CUtensorMap tm_x, const QkvArgs a) {
+  __shared__ __align__(8) uint64_t full_bar[16];
+  __shared__ __align__(8) uint64_t empty_bar[16];
+  __shared__ __align__(8) uint64_t done_bar;
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ RowState rs;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y, m0 = blockIdx.z * kStreamM;
+  const int n0 = tile * kStreamN;
+  const int M = min(a.M - m0, kStreamM);  // rows of this batch tile
+  const int ncols = min(kStreamN, a.n_out - n0);  // a multiple of 64
+  const int BT = a.batch_tile;
+  constexpr uint32_t w_half = kTileN * 128;
+  const uint32_t x_bytes = (uint32_t)BT * 128;
+  const uint32_t stage_bytes = 2 * w_half + x_bytes;
+  // this split's range of 64-wide K blocks
+  const int kb_per = a.kb_total / a.splits, kb_rem = a.kb_total % a.splits;
+  const int kb0 = split * kb_per + min(split, kb_rem);
+  const int nkb = kb_per + (split < kb_rem ? 1 : 0);
+  const bool two = 2 * tile + 1 < a.ntiles_n;  // the tile's second 128-feature chunk exists
+  const int cta_lin = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;  // trace slot
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0 && cta_lin < kTraceMaxCta) a.trace[kTraceCta + 8 * cta_lin + 0] = gtime();
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.nstage; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&done_bar, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_slot)),
+                 "r"(kStreamN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_slot;
+  griddep_launch_dependents();  // the next kernel waits for this grid before reading anything
+
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer: the first ring's worth of weight chunks before
+      // griddepcontrol.wait (the packed weights are never written by the
+      // kernel this one may overlap), x only after it
+      const bool stall = a.inject_stall && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+      const int pre = min(nkb, a.nstage);
+      const unsigned char* w = static_cast<const unsigned char*>(a.w_packed);
+      auto load_w = [&](int i) {
+        const int s = i % a.nstage;
+        unsigned char* st = smem + (size_t)s * stage_bytes;
+        mbar_arrive_expect_tx(&full_bar[s], (two ? 2 : 1) * w_half + x_bytes);
+        bulk_load(st, w + ((size_t)(2 * tile) * a.kb_total + kb0 + i) * w_half, w_half, &full_bar[s]);
+        if (two) bulk_load(st + w_half, w + ((size_t)(2 * tile + 1) * a.kb_total + kb0 + i) * w_half, w_half, &full_bar[s]);
+      };
+      auto load_x = [&](int i) {
+        const int s = i % a.nstage;
+        // 64 elements = 128 bytes: meets the 16-byte rule
+        tma_load_2d(smem + (size_t)s * stage_bytes + 2 * w_half, &tm_x, &full_bar[s], (kb0 + i) * kTileK, m0);
+      };
+      for (int i = (stall ? 1 : 0); i < pre; ++i) load_w(i);  // fresh ring: no empty wait
+      griddep_wait();
+      if constexpr (kTrace) {
+        if (a.trace && true && cta_lin < kTraceMaxCta) a.trace[kTraceCta + 8 * cta_lin + 1] = gtime();
+      }
+      for (int i = (stall ? 1 : 0); i < pre; ++i) load_x(i);  // test hook: stage 0 never filled
+      int issued = pre;
+      for (int i = pre; i < nkb; ++i) {
+        const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
+        if (!mbar_wait_bounded(&empty_bar[i % a.nstage], ph ^ 1u, a.flags, a.wait_limit)) break;
+        load_w(i);
+        load_x(i);
+        ++issued;
+      }
+      // drain: the copies issued last must have landed before shared memory is reused
+      for (int i = max(stall ? 1 : 0, issued - a.nstage); i < issued; ++i)
+        mbar_wait_bounded(&full_bar[i % a.nstage], (uint32_t)(i / a.nstage) & 1u, a.flags, a.wait_limit);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer: A = x rows (rows past the copied batch tile only feed
+      // accumulator rows that are never stored), B = the 256 weight rows
+      const uint32_t idesc = qkv_idesc(bf16, kStreamM, kStreamN);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % a.nstage;
+        const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
+        if (!mbar_wait_bounded(&full_bar[s], ph, a.flags, a.wait_limit)) break;
+        if constexpr (kTrace) {
+          if (a.trace && i == 0 && cta_lin < kTraceMaxCta) a.trace[kTraceCta + 8 * cta_lin + 2] = gtime();
+        }
+        tc_fence_after();
+        const uint32_t sw = smem_u32(smem + (size_t)s * stage_bytes);
+        const uint64_t da = sw128_kmajor_desc(sw + 2 * w_half), db = sw128_kmajor_desc(sw);
+#pragma unroll
+        for (int k = 0; k < kTileK / 16; ++k)  // 16 elements = 32 bytes = 2 descriptor units
+          umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&empty_bar[s]);
+      }
+      umma_commit(&done_bar);
+      if constexpr (kTrace) {
+        if (a.trace && true && cta_lin < kTraceMaxCta) a.trace[kTraceCta + 8 * cta_lin + 3] = gtime();
+      }
+    }
+    __syncwarp();
+  } else {
+    // warps 2-7, idle during the main loop: rows, RoPE factors, this tile's
+    // bias (all read after the barrier below)
+    griddep_wait();
+    init_rows(a, rs, m0, threadIdx.x - 64, kClusterThreads - 64, blockIdx.x == 0 && blockIdx.y == 0);
+    load_tile_bias(a, rs, n0, ncols, threadIdx.x - 64, kClusterThreads - 64);
+  }
+  griddep_wait();  // warps 0-1 (the others have waited already): outputs
+  __syncthreads();
+  mbar_wait_bounded(&done_bar, 0, a.flags, a.wait_limit);
+  tc_fence_after();
+
+  const int g = warp & 3, half = warp >> 2;
+  const int r = g * 32 + lane;  // this thread's batch row while draining
+  const uint32_t t_lane = tmem + ((uint32_t)(g * 32) << 16);
+  const int S = a.splits;
+  const int nchunks = ncols / 16;
+  if (S == 1) {
+    for (int c = half; c < nchunks; c += 2) {
+      float v[16];
+      tmem_ld16(t_lane + (uint32_t)(c * 16), v);
+      if (r < M) emit_chunk<T>(a, rs, m0, r, n0 + c * 16, n0, v);
+    }
+  } else {
+    // rows per owner and the receive buffer, float4s laid out
+    // recv[src][16-feature chunk][quarter][row - lo]: the lanes of a warp
+    // (consecutive rows) write consecutive 16-byte words of a peer's buffer
+    const uint32_t rank = cluster_rank();
+    const int rows_per = (BT + S - 1) / S;
+    float4* recv = reinterpret_cast<float4*>(smem);
+    // every CTA of the cluster has finished its main loop before anyone
+    // writes into another's ring
+    cluster_sync();
+    if constexpr (kTrace) {
+      if (a.trace && threadIdx.x == 0 && cta_lin < kTraceMaxCta) a.trace[kTraceCta + 8 * cta_lin + 5] = gtime();
+    }
+    for (int c = half; c < nchunks; c += 2) {
+      float v[16];
+      tmem_ld16(t_lane + (uint32_t)(c * 16), v);
+      if (r < M) {
+        const int owner = r / rows_per;
+        float4* dst = recv + ((size_t)(rank * (kStreamN / 16) + c) * 4) * rows_per + (r - owner * rows_per);
+        const uint32_t da = map_peer(dst, (uint32_t)owner);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          st_cluster_v4(da + 16u * (uint32_t)(i * rows_per), v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    tc_fence_before();
+    cluster_sync();  // pushes visible; no shared memory is touched remotely after this
+    if constexpr (kTrace) {
+      if (a.trace && threadIdx.x == 0 && cta_lin < kTraceMaxCta) a.trace[kTraceCta + 8 * cta_lin + 6] = gtime();
+    }
+    const int lo = (int)rank * rows_per;
+    const int n_rows = max(0, min(rows_per, M - lo));
+    const int items = n_rows * nchunks;
+    for (int it = threadIdx.x; it < items; it += kClusterThreads) {
+      const int rr = it % n_rows, c = it / n_rows;
+      float sum[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) sum[i] = 0.f;
+      for (int p = 0; p < S; ++p) {
+        const float4* src = recv + ((size_t)(p * (kStreamN / 16) + c) * 4) * rows_per + rr;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 x4 = src[(size_t)i * rows_per];
+          sum[4 * i] += x4.x;
+          sum[4 * i + 1] += x4.y;
+          sum[4 * i + 2] += x4.z;
+          sum[4 * i + 3] += x4.w;
+        }
+      }
+      emit_chunk<T>(a, rs, m0, lo + rr, n0 + c * 16, n0, sum);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0 && cta_lin < kTraceMaxCta) a.trace[kTraceCta + 8 * cta_lin + 4] = gtime();
+  }
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kStreamN) : "memory");
   }
 }
 
@@ -758,13 +1000,14 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
 using namespace clove;
 
 // Clusters of `splits` CTAs of this kernel that fit on the GPU at once,
-// cached per (device, dtype, splits, shared memory).
+// cached per (device, kernel kind, splits, shared memory); kind tells the
+// kernels and their element types apart.
 template <typename Kern>
-static int resident_clusters(Kern kern, const cudaLaunchConfig_t& cfg, int device, int dtype, int splits,
+static int resident_clusters(Kern kern, const cudaLaunchConfig_t& cfg, int device, int kind, int splits,
                              size_t smem) {
   static std::mutex mu;
   static std::map<std::tuple<int, int, int, size_t>, int> cache;
-  const auto key = std::make_tuple(device, dtype, splits, smem);
+  const auto key = std::make_tuple(device, kind, splits, smem);
   {
     std::lock_guard<std::mutex> g(mu);
     auto it = cache.find(key);
@@ -828,7 +1071,8 @@ static size_t packed_bytes(int n_out, int hidden) {
 
 // Schedule and workspace of one call.
 struct QkvPlan {
-  bool stream_k;  // false: the cluster schedule
+  bool stream_k;   // the stream-K schedule (weights in N)
+  bool cluster_n;  // the cluster schedule with the weights in N (else, without stream_k: in M)
   int batch_tile, ntiles_n, n_btiles, kb_total, grid, max_contrib, nstage;
   long long units;
   size_t smem, off_partials, ws_bytes;
@@ -849,8 +1093,44 @@ static QkvPlan plan_qkv(const clove_pool& pool, int batch, int hidden, int num_q
   const int n_out = (num_q_heads + 2 * pool.num_kv_heads) * pool.head_dim;
   P.ntiles_n = (n_out + kTileN - 1) / kTileN;
   P.kb_total = (hidden + kTileK - 1) / kTileK;
-  P.stream_k = batch <= kStreamMaxBatch;
-  if (P.stream_k) {
+  // Weights in N (256-feature tiles) up to 128 batch rows.  The cluster
+  // schedule when its clusters cover 90 % of the SMs or the batch is above
+  // 32 rows (stream-K partials grow with the batch); stream-K otherwise.
+  {
+    const int tiles = (P.ntiles_n + 1) / 2;
+    const int s_fit = std::max(1, std::min({pool.num_sms / tiles, 8, std::max(1, P.kb_total / 2)}));
+    const bool covers = 10 * tiles * s_fit >= 9 * pool.num_sms;
+    const int mt = (batch + kStreamM - 1) / kStreamM;
+    const int s_fit_m = std::max(1, std::min({pool.num_sms / (tiles * mt), 8, std::max(1, P.kb_total / 2)}));
+    const bool covers_m = 10 * tiles * mt * s_fit_m >= 9 * pool.num_sms;
+    P.cluster_n = batch <= kStreamM ? (batch > kStreamMaxBatch || covers || tiles >= pool.num_sms) : covers_m;
+    P.stream_k = batch <= kStreamMaxBatch && !P.cluster_n;
+    // CLOVE_QKV_SCHEDULE = stream | cluster_n | cluster_m forces a schedule
+    // (a tuning override, read once; stream only up to 128 batch rows)
+    static const int forced = [] {
+      const char* v = std::getenv("CLOVE_QKV_SCHEDULE");
+      if (!v) return 0;
+      const std::string t(v);
+      return t == "stream" ? 1 : t == "cluster_n" ? 2 : t == "cluster_m" ? 3 : 0;
+    }();
+    if (forced) {
+      P.stream_k = forced == 1 && batch <= kStreamM;
+      P.cluster_n = forced == 2 || (forced == 1 && !P.stream_k);
+    }
+  }
+  if (P.cluster_n) {
+    P.n_btiles = (batch + kStreamM - 1) / kStreamM;
+    P.batch_tile = P.n_btiles > 1 ? kStreamM : ((batch + 15) / 16) * 16;
+    P.units = (long long)((P.ntiles_n + 1) / 2) * P.kb_total;
+    const size_t stage = 2 * (size_t)kTileN * 128 + (size_t)P.batch_tile * 128;
+    const size_t pad = (size_t)(kStreamM - P.batch_tile) * 128;
+    P.nstage = (int)std::max<size_t>(2, std::min<size_t>(16, ring_budget(kSmemBudget - pad) / stage));
+    P.smem = stage * P.nstage + pad + 1024;
+    P.grid = 0;  // splits chosen at launch (cluster occupancy)
+    P.max_contrib = 0;
+    P.off_partials = 0;
+    P.ws_bytes = 256;  // no workspace
+  } else if (P.stream_k) {
     // (256-feature tile) x (64-wide K block) units, split evenly and
     // contiguously over one CTA per SM, at least two K blocks each
     P.n_btiles = 1;
@@ -1012,6 +1292,42 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x, const void* w_packed
       attr[0].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
+      e = cudaLaunchKernelEx(&cfg, kern, tm_x, a);
+    }
+  } else if (P.cluster_n) {
+    auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_cluster_n_kernel<__nv_bfloat16> : qkv_cluster_n_kernel<__half>;
+    const int tiles = (P.ntiles_n + 1) / 2;
+    const size_t stage = 2 * (size_t)kTileN * 128 + (size_t)P.batch_tile * 128;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kClusterThreads);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cfg.dynamicSmemBytes = P.smem;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;  // the occupancy query sees the cluster shape only
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem);
+    // K splits: enough CTAs to cover the SMs, at most 8 (portable cluster),
+    // at least 2 K blocks each, a receive buffer of splits x (rows per CTA) x
+    // 256 f32 that fits in the ring, and all clusters resident at once
+    const int mt = P.n_btiles;
+    int splits = std::max(1, std::min({pool->num_sms / (tiles * mt), 8, std::max(1, P.kb_total / 2)}));
+    for (; e == cudaSuccess && splits > 1; --splits) {
+      const size_t rows_per = ((size_t)P.batch_tile + splits - 1) / splits;
+      if ((size_t)splits * rows_per * kStreamN * 4 > stage * P.nstage) continue;
+      cfg.gridDim = dim3(tiles, splits, mt);
+      attr[0].val.clusterDim.y = splits;
+      if (resident_clusters(kern, cfg, pool->device, 16 + (int)pool->dtype, splits, P.smem) >= tiles * mt) break;
+    }
+    a.splits = splits;
+    if (e == cudaSuccess) {
+      cfg.gridDim = dim3(tiles, splits, mt);
+      attr[0].val.clusterDim.y = splits;
+      cfg.numAttrs = 2;
       e = cudaLaunchKernelEx(&cfg, kern, tm_x, a);
     }
   } else {
