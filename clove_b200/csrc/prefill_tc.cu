@@ -93,18 +93,6 @@ __device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
   return __uint_as_float(r);
 }
 
-// A whole 128-column row of this thread's lane.
-__device__ __forceinline__ void tmem_ld_row128(uint32_t taddr, float (&v)[128]) {
-  uint32_t r[8][16];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tmem_ld16_async(taddr + 16 * i, r[i]);
-  tmem_ld_wait();
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int k = 0; k < 16; ++k) v[16 * i + k] = __uint_as_float(r[i][k]);
-}
-
 // 2^x with the tensor-core path's accuracy needs (P is rounded to 16 bits
 // next): the special-function unit's approximation, -inf -> +0.
 __device__ __forceinline__ float ex2_approx(float x) {

@@ -10,43 +10,46 @@
 // and stores k, v straight into their cache slots, so K/V never make a round
 // trip through global memory.
 //
-// Shape of the work.  At decode the batch (M = 1..256 tokens per batch tile)
-// is small and the weights W [hidden, (Hq + 2 Hkv) D] are large: the kernel
-// streams the weights once, so HBM bandwidth bounds it.  The product is
-// computed transposed, D^T = W^T x^T: the 128-row tensor-core tile runs over
-// output features and the batch is the MMA's N dimension (16..256).
+// Shape of the work.  At decode the batch is small and the weights W
+// [hidden, (Hq + 2 Hkv) D] are large: the kernel streams the weights once,
+// so HBM bandwidth bounds it.  Every tcgen05.mma costs about the same issue
+// time whatever its shape, so the weights ride in the MMA's N operand: a
+// tile is 256 output features (N = 256, 8 KB of weights per K = 16 step)
+// against up to 128 batch rows (M = 128; x rows past the batch tile only
+// feed accumulator rows that are never stored).  With the weights in M (4 KB
+// per instruction) the tensor pipe, not HBM, set the streaming rate.  The
+// accumulator holds batch row b in tensor-memory lane b and feature f in
+// column f, so an epilogue thread writes 16 consecutive features (32 bytes)
+// of a q row or cache slot at a time.
 //
 // Weight layout.  W^T is packed once (clove_cuda_qkv_pack_weights) into
-// 128-feature x 64-element tiles, each a contiguous 16 KB chunk already in the
-// 128-byte-swizzled K-major order the tensor cores read, so one (feature
-// tile, K block) is one plain bulk copy and a CTA streams consecutive chunks
-// (row-strided tensor-map boxes cost DRAM page locality once every SM
-// streams).  x, small and L2-resident, comes through a 2-D tensor map with
-// the same swizzle.
+// 128-feature x 64-element chunks, each a contiguous 16 KB block already in
+// the 128-byte-swizzled K-major order the tensor cores read; a stage takes
+// two of them (the tile's two halves at one K block) with plain bulk copies.
+// x, small and L2-resident, comes through a 2-D tensor map with the same
+// swizzle.
 //
-// Two schedules, by batch tile:
-//  - up to 32 columns (64 when clusters would leave SMs idle), stream-K
-//    (qkv_append_kernel): (feature tile) x (batch
-//    tile) x (64-wide K block) units split evenly and contiguously over one
-//    CTA per SM, so every SM streams whatever the tile count.  A CTA's range
-//    covers pieces ("segments") of one or more tiles.  A whole-tile segment
-//    goes straight to the epilogue; otherwise its f32 partial goes to a
-//    workspace slot, and the CTA that completes the tile's last piece (a
-//    per-tile arrival counter, reset by that CTA) sums the partials in slot
-//    order and runs the epilogue.  192 threads: warp 0 lane 0 issues the
-//    copies into a ring of stages; warp 1 lane 0 issues tcgen05.mma into one
-//    of two tensor-memory accumulators (one segment drains while the next
-//    accumulates) and commits stages back; warps 2-5 (tensor-memory lane
-//    groups 2, 3, 0, 1: one output feature per thread) run the epilogue.
-//  - larger tiles, a cluster schedule (qkv_cluster_kernel): the K splits of
-//    a feature tile form a thread-block cluster and reduce through
-//    distributed shared memory, each CTA finishing a slice of the columns —
-//    at large tiles the partials are too big for one CTA to sum.
-// The epilogue adds the bias, rotates, rounds, stages a tile's columns in
-// shared memory and writes each column's 128 features — contiguous in q's
-// row or in the cache slot row — as 16-byte stores.  Every wait is bounded;
-// a wait that runs out sets CLOVE_FLAG_TIMEOUT in the pool's flag word and
-// the CTA finishes without hanging.
+// Two schedules:
+//  - cluster (qkv_cluster_n_kernel), the usual one: grid (feature tiles) x
+//    (K splits) x (128-row batch tiles), the K splits of a tile forming one
+//    thread-block cluster sized so that every cluster is resident and the
+//    CTAs cover the SMs.  After the main loops the split-K partial sums meet
+//    in distributed shared memory, each CTA of the cluster adding and
+//    storing its slice of the batch rows.
+//  - stream-K (qkv_stream_kernel), for batches up to 32 rows when the
+//    clusters would leave over 40 % of the SMs idle: (feature tile) x
+//    (64-wide K block) units split evenly and contiguously over one CTA per
+//    SM.  A CTA's range covers pieces ("segments") of one or more tiles; a
+//    whole-tile segment goes straight to the epilogue, otherwise its f32
+//    partial goes to a workspace slot and the CTA that completes the tile's
+//    last piece (a per-tile arrival counter, reset by that CTA) sums the
+//    slots in order and runs the epilogue.
+// Both are programmatic dependents of the previous kernel on the stream: the
+// barrier set-up, tensor-memory allocation and the first ring of weight
+// copies run before griddepcontrol.wait.  The epilogue adds the bias,
+// rotates (RoPE), rounds and stores q and the K/V slot rows.  Every wait is
+// bounded; a wait that runs out sets CLOVE_FLAG_TIMEOUT in the pool's flag
+// word and the CTA finishes without hanging.
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
@@ -65,18 +68,16 @@ namespace clove {
 
 namespace {
 
-constexpr int kQkvThreads = 192;  // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
+constexpr int kQkvThreads = 192;      // stream-K: warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
 constexpr int kEpiThreads = 128;
 constexpr int kClusterThreads = 256;  // cluster schedule: warp 0 copies, warp 1 MMAs, all 8 in the epilogue
-constexpr int kStreamMaxBatch = 32;   // batches up to this use the stream-K kernel (its M is 128 rows)
-constexpr int kStreamM = 128;         // stream-K: batch rows per tile (MMA M)
-constexpr int kStreamN = 256;         // stream-K: output features per tile (MMA N)
+constexpr int kStreamMaxBatch = 32;   // stream-K only up to this batch (its partials grow with the batch)
+constexpr int kStreamM = 128;         // batch rows per tile (MMA M)
+constexpr int kStreamN = 256;         // output features per tile (MMA N: two packed 128-feature chunks)
 constexpr int kMaxHeadDim = 256;
-constexpr size_t kRingBudget = 200 * 1024;  // cluster schedule: ring bytes (its epilogue buffers overlay it)
-constexpr int kTileN = 128;       // output features per tile (tensor-core M)
-constexpr int kTileK = 64;        // hidden elements per stage (one 128-byte swizzle row)
-constexpr int kMaxBatchTile = 256;
-constexpr size_t kSmemBudget = 224 * 1024;  // ring + output staging
+constexpr int kTileN = 128;           // features per packed weight chunk
+constexpr int kTileK = 64;            // hidden elements per stage (one 128-byte swizzle row)
+constexpr size_t kSmemBudget = 224 * 1024;  // stage ring + padding
 
 struct QkvArgs {
   const void* w_packed;         // [ntiles_n][kb_total][128][64] pre-swizzled
@@ -139,12 +140,6 @@ template <typename T>
 __device__ __forceinline__ T to_elem(float x);
 template <> __device__ __forceinline__ __nv_bfloat16 to_elem<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 template <> __device__ __forceinline__ __half to_elem<__half>(float x) { return __float2half_rn(x); }
-
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // First CTA whose unit range [g*U/G, (g+1)*U/G) contains unit x.
 __device__ __forceinline__ int first_cta(long long x, long long units, int grid) {
@@ -746,253 +741,6 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
   }
 }
 
-// Cluster schedule for batches above 128: grid (feature tiles) x
-// (K splits) x (batch tiles), the K splits of a feature tile forming one
-// thread-block cluster.  Each CTA accumulates its K range in tensor memory;
-// the CTAs then push each other's columns through distributed shared memory
-// (CTA j owns a 1/splits slice of the batch columns) and each runs the
-// epilogue for its slice, so the reduction is spread over the cluster.
-// 256 threads: warp 0 copies, warp 1 MMAs, warps 2-7 look up the cache slots;
-// all 8 warps drain (warp w reads tensor-memory lanes 32 (w % 4) .., for
-// alternating 16-column chunks) and store.
-template <typename T>
-__global__ void __launch_bounds__(kClusterThreads, 1)
-    qkv_cluster_kernel(const __grid_constant__ CUtensorMap tm_x, const QkvArgs a) {
-  __shared__ __align__(8) uint64_t full_bar[16];
-  __shared__ __align__(8) uint64_t empty_bar[16];
-  __shared__ __align__(8) uint64_t done_bar;
-  __shared__ uint32_t tmem_base_slot;
-  __shared__ int32_t slot_of[kMaxBatchTile];  // cache row of each batch column (-1: skip)
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile_n = blockIdx.x, split = blockIdx.y, tile_m = blockIdx.z;
-  const int n0 = tile_n * kTileN, m0 = tile_m * kMaxBatchTile;
-  const int BT = a.batch_tile;
-  const uint32_t a_bytes = kTileN * 128, b_bytes = (uint32_t)BT * 128;
-  const uint32_t stage_bytes = a_bytes + b_bytes;
-  // this split's range of 64-wide K blocks
-  const int kb_per = a.kb_total / a.splits, kb_rem = a.kb_total % a.splits;
-  const int kb0 = split * kb_per + min(split, kb_rem);
-  const int nkb = kb_per + (split < kb_rem ? 1 : 0);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < a.nstage; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
-    }
-    mbar_init(&done_bar, 1);
-    fence_barrier_init();
-  }
-  __syncwarp();
-  if (warp == 0) {
-    // tensor-memory columns: a power of two >= 32 covering the batch tile
-    const uint32_t ncols = BT <= 32 ? 32u : BT <= 64 ? 64u : BT <= 128 ? 128u : 256u;
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_slot)),
-                 "r"(ncols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_base_slot;
-  // the next kernel on the stream may be scheduled now (it waits for this
-  // grid before reading anything)
-  griddep_launch_dependents();
-
-  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-  if (warp == 0) {
-    if (lane == 0) {
-      // producer: W^T tile [128 features, 64] and x tile [BT, 64] per stage;
-      // the first ring's worth of weight chunks before griddepcontrol.wait
-      // (the packed weights are never written by the kernel this one may
-      // overlap), x only after it
-      const bool stall = a.inject_stall && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
-      const int pre = min(nkb, a.nstage);
-      auto load_w = [&](int i) {
-        unsigned char* st = smem + (size_t)(i % a.nstage) * stage_bytes;
-        mbar_arrive_expect_tx(&full_bar[i % a.nstage], stage_bytes);
-        // the weight chunk of (feature tile, K block): 16 KB, contiguous, pre-swizzled
-        bulk_load(st, static_cast<const unsigned char*>(a.w_packed) + ((size_t)tile_n * a.kb_total + kb0 + i) * a_bytes,
-                  a_bytes, &full_bar[i % a.nstage]);
-      };
-      auto load_x = [&](int i) {
-        const int k0 = (kb0 + i) * kTileK;  // 64 elements = 128 bytes: meets the 16-byte rule
-        tma_load_2d(smem + (size_t)(i % a.nstage) * stage_bytes + a_bytes, &tm_x, &full_bar[i % a.nstage], k0, m0);
-      };
-      for (int i = (stall ? 1 : 0); i < pre; ++i) load_w(i);  // fresh ring: no empty wait
-      griddep_wait();
-      for (int i = (stall ? 1 : 0); i < pre; ++i) load_x(i);  // test hook: stage 0 never filled
-      int issued = pre;
-      for (int i = pre; i < nkb; ++i) {
-        const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
-        if (!mbar_wait_bounded(&empty_bar[i % a.nstage], ph ^ 1u, a.flags, a.wait_limit)) break;
-        load_w(i);
-        load_x(i);
-        ++issued;
-      }
-      // drain: the copies issued last must have landed before shared memory is reused
-      for (int i = max(stall ? 1 : 0, issued - a.nstage); i < issued; ++i)
-        mbar_wait_bounded(&full_bar[i % a.nstage], (uint32_t)(i / a.nstage) & 1u, a.flags, a.wait_limit);
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // MMA issuer
-      const uint32_t idesc = qkv_idesc(bf16, kTileN, BT);
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % a.nstage;
-        const uint32_t ph = (uint32_t)(i / a.nstage) & 1u;
-        if (!mbar_wait_bounded(&full_bar[s], ph, a.flags, a.wait_limit)) break;
-        tc_fence_after();
-        const uint32_t sa = smem_u32(smem + (size_t)s * stage_bytes);
-        const uint64_t da = sw128_kmajor_desc(sa), db = sw128_kmajor_desc(sa + a_bytes);
-#pragma unroll
-        for (int k = 0; k < kTileK / 16; ++k)  // 16 elements = 32 bytes = 2 descriptor units
-          umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&empty_bar[s]);
-      }
-      umma_commit(&done_bar);
-    }
-    __syncwarp();
-  } else {
-    // warps 2-7, idle during the main loop: the cache slot of each batch
-    // column from its sequence's block table (read after the barrier below)
-    griddep_wait();
-    for (int c = threadIdx.x - 64; c < BT; c += kClusterThreads - 64) {  // warps 2-7
-      const int b = m0 + c;
-      int slot = -1;
-      if (b < a.M) {
-        const int pos = __ldg(a.context_lens + b);
-        if (pos < 0 || pos / a.bs >= a.bt_stride) {
-          atomicOr(a.flags, CLOVE_FLAG_CTX_RANGE);
-        } else {
-          const int phys = __ldg(a.block_tables + (size_t)b * a.bt_stride + pos / a.bs);
-          if (phys < 0 || phys >= a.num_blocks) atomicOr(a.flags, CLOVE_FLAG_BLOCK_OOB);
-          else slot = phys * a.bs + pos % a.bs;
-        }
-        if (a.lens_out && tile_n == 0 && split == 0) a.lens_out[b] = pos + 1;
-      }
-      slot_of[c] = slot;
-    }
-  }
-
-  griddep_wait();  // warps 0-1 (the others have waited already): bias, context lengths, outputs
-
-  // ---- epilogue.  Thread t computes feature r = t % 128 (its tensor-memory
-  // lane) for the columns of its half h = t / 128 (alternating 16-column
-  // chunks), rounds, and stages the result in shared memory as
-  // stage[c][128] (pool dtype); the CTA then writes each column's 128
-  // features — contiguous in q's row or in the cache slot row — as 16-byte
-  // vectors.
-  const int r = threadIdx.x & (kTileN - 1), half = threadIdx.x >> 7;
-  const int f = n0 + r;
-  const int qd = a.hq * a.D, kd = a.hkv * a.D;
-  const float bias = (a.bias && f < a.n_out) ? __ldg(a.bias + f) : 0.f;
-  const int d = f % a.D;
-  // RoPE angle factor for this feature's pair (2i, 2i+1): theta^(-2i/D)
-  // (warp-uniform: a warp's 32 features never straddle a head boundary)
-  const bool rot = a.rope_theta > 0.f && f < qd + kd;
-  const float inv_freq = rot ? powf(a.rope_theta, -2.f * (float)(d >> 1) / (float)a.D) : 0.f;
-  auto finish = [&](int c, float val) -> T {  // c: column within the batch tile
-    val += bias;
-    if (rot) {
-      // partner element of the pair lives in the neighbouring lane
-      const float other = __shfl_xor_sync(0xffffffffu, val, 1);
-      const int b = m0 + c;
-      const int pos = b < a.M ? __ldg(a.context_lens + b) : 0;
-      float sn, cs;
-      sincosf((float)pos * inv_freq, &sn, &cs);
-      val = (d & 1) ? other * sn + val * cs : val * cs - other * sn;
-    }
-    return to_elem<T>(val);
-  };
-
-  mbar_wait_bounded(&done_bar, 0, a.flags, a.wait_limit);
-  tc_fence_after();
-  const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-  const int S = a.splits;
-  int c_lo = 0, n_c = BT;  // this CTA's columns
-  T* stage_out;
-  if (S == 1) {
-    stage_out = reinterpret_cast<T*>(smem);
-    for (int c0 = 16 * half; c0 < BT; c0 += 32) {
-      float v[16];
-      tmem_ld16(t_lane + (uint32_t)c0, v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) stage_out[(c0 + i) * kTileN + r] = finish(c0 + i, v[i]);
-    }
-    tc_fence_before();
-    __syncthreads();  // staging and slot_of complete
-  } else {
-    // ---- split-K reduction across the cluster.  CTA j owns the batch
-    // columns [j*cs, (j+1)*cs) (cs a multiple of 16); every CTA pushes its
-    // partial sums of those columns into CTA j's receive buffer
-    // recv[src][feature][cs + 4] (f32, overlaying the ring; the 4-float pad
-    // keeps 16-byte accesses of consecutive features on distinct banks), so
-    // each value crosses the cluster once, with 16-byte stores.
-    const uint32_t rank = cluster_rank();
-    const int cs = ((BT + S - 1) / S + 15) & ~15;
-    const int pitch = cs + 4;
-    float* recv = reinterpret_cast<float*>(smem);
-    stage_out = reinterpret_cast<T*>(smem + (size_t)S * kTileN * pitch * 4);
-    // every CTA of the cluster has finished its main loop before anyone
-    // writes into another's ring
-    cluster_sync();
-    for (int c0 = 16 * half; c0 < BT; c0 += 32) {
-      float v[16];
-      tmem_ld16(t_lane + (uint32_t)c0, v);
-      const int owner = c0 / cs;
-      float* dst = recv + ((size_t)rank * kTileN + r) * pitch + (c0 - owner * cs);
-      const uint32_t da = map_peer(dst, (uint32_t)owner);
-#pragma unroll
-      for (int i = 0; i < 16; i += 4) st_cluster_v4(da + 4u * i, v[i], v[i + 1], v[i + 2], v[i + 3]);
-    }
-    tc_fence_before();
-    cluster_sync();  // pushes visible; no shared memory is touched remotely after this
-    c_lo = (int)rank * cs;
-    n_c = max(0, min(cs, BT - c_lo));
-    for (int j = 4 * half; j < n_c; j += 8) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int p = 0; p < S; ++p) {
-        const float4 x4 = *reinterpret_cast<const float4*>(recv + ((size_t)p * kTileN + r) * pitch + j);
-        acc.x += x4.x; acc.y += x4.y; acc.z += x4.z; acc.w += x4.w;
-      }
-      stage_out[(j + 0) * kTileN + r] = finish(c_lo + j + 0, acc.x);
-      stage_out[(j + 1) * kTileN + r] = finish(c_lo + j + 1, acc.y);
-      stage_out[(j + 2) * kTileN + r] = finish(c_lo + j + 2, acc.z);
-      stage_out[(j + 3) * kTileN + r] = finish(c_lo + j + 3, acc.w);
-    }
-    __syncthreads();
-  }
-  // ---- 16-byte stores: 16 chunks of 8 features per column.  Section
-  // boundaries (q | k | v) are multiples of 64 features, so a chunk never
-  // straddles one.
-  for (int q = threadIdx.x; q < n_c * 16; q += kClusterThreads) {
-    const int cl = q >> 4, f0 = n0 + (q & 15) * 8;
-    const int b = m0 + c_lo + cl;
-    if (b >= a.M || f0 >= a.n_out) continue;
-    const uint4 val = *reinterpret_cast<const uint4*>(stage_out + (size_t)cl * kTileN + (q & 15) * 8);
-    T* dst;
-    if (f0 < qd) {
-      dst = static_cast<T*>(a.q_out) + (size_t)b * qd + f0;
-    } else {
-      const int slot = slot_of[c_lo + cl];
-      if (slot < 0) continue;
-      const bool is_k = f0 < qd + kd;
-      dst = static_cast<T*>(is_k ? a.k_cache : a.v_cache) + (size_t)slot * kd + (f0 - (is_k ? qd : qd + kd));
-    }
-    __stcs(reinterpret_cast<uint4*>(dst), val);
-  }
-  if (warp == 0) {
-    tc_fence_after();
-    const uint32_t ncols = BT <= 32 ? 32u : BT <= 64 ? 64u : BT <= 128 ? 128u : 256u;
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
-  }
-}
-
 }  // namespace
 
 }  // namespace clove
@@ -1071,8 +819,8 @@ static size_t packed_bytes(int n_out, int hidden) {
 
 // Schedule and workspace of one call.
 struct QkvPlan {
-  bool stream_k;   // the stream-K schedule (weights in N)
-  bool cluster_n;  // the cluster schedule with the weights in N (else, without stream_k: in M)
+  bool stream_k;   // the stream-K schedule
+  bool cluster_n;  // the cluster schedule (exactly one of the two is set)
   int batch_tile, ntiles_n, n_btiles, kb_total, grid, max_contrib, nstage;
   long long units;
   size_t smem, off_partials, ws_bytes;
@@ -1093,30 +841,24 @@ static QkvPlan plan_qkv(const clove_pool& pool, int batch, int hidden, int num_q
   const int n_out = (num_q_heads + 2 * pool.num_kv_heads) * pool.head_dim;
   P.ntiles_n = (n_out + kTileN - 1) / kTileN;
   P.kb_total = (hidden + kTileK - 1) / kTileK;
-  // Weights in N (256-feature tiles) up to 128 batch rows.  The cluster
-  // schedule when its clusters cover 90 % of the SMs or the batch is above
-  // 32 rows (stream-K partials grow with the batch); stream-K otherwise.
+  // The cluster schedule when its CTAs (256-feature tiles x 128-row batch
+  // tiles x K splits, at most 8) cover 60 % of the SMs or the batch is above
+  // 32 rows; stream-K (one CTA per SM whatever the tile count) otherwise.
   {
-    const int tiles = (P.ntiles_n + 1) / 2;
-    const int s_fit = std::max(1, std::min({pool.num_sms / tiles, 8, std::max(1, P.kb_total / 2)}));
-    const bool covers = 10 * tiles * s_fit >= 9 * pool.num_sms;
-    const int mt = (batch + kStreamM - 1) / kStreamM;
-    const int s_fit_m = std::max(1, std::min({pool.num_sms / (tiles * mt), 8, std::max(1, P.kb_total / 2)}));
-    const bool covers_m = 10 * tiles * mt * s_fit_m >= 9 * pool.num_sms;
-    P.cluster_n = batch <= kStreamM ? (batch > kStreamMaxBatch || covers || tiles >= pool.num_sms) : covers_m;
-    P.stream_k = batch <= kStreamMaxBatch && !P.cluster_n;
-    // CLOVE_QKV_SCHEDULE = stream | cluster_n | cluster_m forces a schedule
-    // (a tuning override, read once; stream only up to 128 batch rows)
+    const int tiles = (P.ntiles_n + 1) / 2, mt = (batch + kStreamM - 1) / kStreamM;
+    const int s_fit = std::max(1, std::min({pool.num_sms / (tiles * mt), 8, std::max(1, P.kb_total / 2)}));
+    const bool covers = 10 * tiles * mt * s_fit >= 6 * pool.num_sms;
+    P.cluster_n = batch > kStreamMaxBatch || covers;
+    // CLOVE_QKV_SCHEDULE = stream | cluster forces a schedule (a tuning
+    // override, read once; stream-K only up to 128 batch rows)
     static const int forced = [] {
       const char* v = std::getenv("CLOVE_QKV_SCHEDULE");
       if (!v) return 0;
       const std::string t(v);
-      return t == "stream" ? 1 : t == "cluster_n" ? 2 : t == "cluster_m" ? 3 : 0;
+      return t == "stream" ? 1 : t == "cluster" ? 2 : 0;
     }();
-    if (forced) {
-      P.stream_k = forced == 1 && batch <= kStreamM;
-      P.cluster_n = forced == 2 || (forced == 1 && !P.stream_k);
-    }
+    if (forced) P.cluster_n = forced == 2 || batch > kStreamM;
+    P.stream_k = !P.cluster_n;
   }
   if (P.cluster_n) {
     P.n_btiles = (batch + kStreamM - 1) / kStreamM;
@@ -1148,16 +890,6 @@ static QkvPlan plan_qkv(const clove_pool& pool, int batch, int hidden, int num_q
     P.smem = stage * P.nstage + pad + 1024;
     P.off_partials = ((size_t)tiles * 4 + 255) & ~size_t(255);
     P.ws_bytes = P.off_partials + (size_t)tiles * P.max_contrib * P.batch_tile * kStreamN * 4;
-  } else {
-    P.n_btiles = (batch + kMaxBatchTile - 1) / kMaxBatchTile;
-    P.batch_tile = P.n_btiles > 1 ? kMaxBatchTile : ((batch + 15) / 16) * 16;
-    P.units = (long long)P.ntiles_n * P.n_btiles * P.kb_total;
-    P.grid = 0;  // chosen at launch (cluster occupancy)
-    P.max_contrib = 0;
-    P.nstage = 0;
-    P.smem = 0;
-    P.off_partials = 0;
-    P.ws_bytes = 256;  // the cluster schedule needs no workspace
   }
   return P;
 }
@@ -1326,50 +1058,6 @@ int clove_cuda_qkv_append(clove_pool_t pool, const void* x, const void* w_packed
     a.splits = splits;
     if (e == cudaSuccess) {
       cfg.gridDim = dim3(tiles, splits, mt);
-      attr[0].val.clusterDim.y = splits;
-      cfg.numAttrs = 2;
-      e = cudaLaunchKernelEx(&cfg, kern, tm_x, a);
-    }
-  } else {
-    auto kern = pool->dtype == CLOVE_DTYPE_BF16 ? qkv_cluster_kernel<__nv_bfloat16> : qkv_cluster_kernel<__half>;
-    const int ntiles = P.ntiles_n;
-    const size_t stage = (size_t)kTileN * 128 + (size_t)P.batch_tile * 128;
-    a.nstage = (int)std::max<size_t>(2, std::min<size_t>(16, ring_budget(kRingBudget) / stage));
-    cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(kClusterThreads);
-    cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // as above
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;  // the occupancy query below sees the cluster shape only
-    // K splits: enough CTAs to cover the SMs, at most 8 (portable cluster),
-    // at least 2 K blocks each, and few enough clusters to be resident at
-    // once (a second wave would double the time)
-    int splits = std::max(1, std::min({pool->num_sms / (ntiles * P.n_btiles), 8, std::max(1, P.kb_total / 2)}));
-    size_t smem = 0;
-    for (; splits >= 1; --splits) {
-      // the epilogue's buffers overlay the ring and must fit in it: the
-      // receive buffer [splits][128][cs + 4] f32 (cs the columns per CTA
-      // rounded up to 16) and the output staging [cs][128]
-      const size_t cs = (((size_t)P.batch_tile + splits - 1) / splits + 15) & ~size_t(15);
-      const size_t recv = splits > 1 ? (size_t)splits * kTileN * (cs + 4) * 4 : 0;
-      if (recv + cs * kTileN * 2 > stage * a.nstage) continue;
-      smem = stage * a.nstage + 1024;
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess || splits == 1) break;
-      cfg.gridDim = dim3(ntiles, splits, P.n_btiles);
-      cfg.dynamicSmemBytes = smem;
-      attr[0].val.clusterDim.y = splits;
-      if (resident_clusters(kern, cfg, pool->device, (int)pool->dtype, splits, smem) >= ntiles * P.n_btiles) break;
-    }
-    a.splits = splits;
-    if (e == cudaSuccess) {
-      cfg.gridDim = dim3(ntiles, splits, P.n_btiles);
-      cfg.dynamicSmemBytes = smem;
       attr[0].val.clusterDim.y = splits;
       cfg.numAttrs = 2;
       e = cudaLaunchKernelEx(&cfg, kern, tm_x, a);

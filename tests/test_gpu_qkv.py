@@ -84,15 +84,15 @@ def _run(dtype, B, hidden, hq, hkv, D, bs, theta, with_bias=True, seed=0):
 @pytest.mark.parametrize("B,hidden,hq,hkv,D,bs,theta", [
     (128, 4096, 32, 8, 128, 16, 0.0),      # C3-shaped decode step
     (128, 4096, 32, 8, 128, 16, 10000.0),  # with RoPE
-    (5, 512, 8, 2, 64, 16, 500.0),         # tiny ragged batch (one MMA N of 16)
-    (300, 1024, 16, 4, 128, 32, 0.0),      # two batch tiles
+    (5, 512, 8, 2, 64, 16, 500.0),         # tiny ragged batch (x tile of 16 rows)
+    (300, 1024, 16, 4, 128, 32, 0.0),      # three 128-row batch tiles
     (33, 520, 4, 4, 64, 8, 10000.0),       # hidden not a multiple of 64 (zero-filled tail)
     (64, 8192, 64, 8, 128, 16, 0.0),       # 70B-shaped projection
     (7, 384, 3, 1, 64, 16, 10000.0),       # 320 features: a partial last tile, q/k boundary mid-tile
-    (140, 384, 3, 1, 64, 16, 10000.0),     # the same through the cluster schedule
+    (140, 384, 3, 1, 64, 16, 10000.0),     # the same through the cluster schedule (two batch tiles)
     (1, 4096, 32, 8, 128, 16, 10000.0),    # batch 1: one live row of the 128-row tile
     (100, 2048, 16, 8, 128, 16, 0.0),      # ragged batch tile of 112 rows
-    (16, 8192, 64, 8, 128, 16, 10000.0),   # stream-K over 40 tiles of 256 features
+    (16, 8192, 8, 2, 128, 16, 10000.0),    # stream-K: 6 tiles over 148 CTAs, ~25 pieces per tile
 ])
 def test_qkv_append_matches_oracle(dtype, B, hidden, hq, hkv, D, bs, theta):
     _run(dtype, B, hidden, hq, hkv, D, bs, theta, seed=B + hidden)
@@ -102,7 +102,7 @@ def test_qkv_append_without_bias():
     _run(torch.bfloat16, 16, 256, 4, 2, 128, 16, 0.0, with_bias=False, seed=3)
 
 
-@pytest.mark.parametrize("pad", [0, 38, 138])  # batch 2 (stream-K), 40 (clusters, weights in N), 140 (weights in M)
+@pytest.mark.parametrize("pad", [0, 38, 138])  # batch 2 (stream-K), 40 and 140 (cluster schedule, 1 and 2 batch tiles)
 def test_qkv_append_flags_bad_slots_and_rejects_f32(pad):
     from clove_b200 import KVPool, _lib
     dev = torch.device("cuda", 0)
@@ -164,7 +164,7 @@ def test_fused_module_forward_matches_unfused(theta):
     assert ok, worst
 
 
-@pytest.mark.parametrize("B", [5, 64, 160])  # stream-K and the two cluster schedules
+@pytest.mark.parametrize("B", [5, 64, 160])  # stream-K, and the cluster schedule with 1 and 2 batch tiles
 def test_stuck_wait_times_out_and_next_call_is_correct(B):
     # Failure detection without a GPU fault: the test hook leaves the first
     # stage of the first CTA unfilled, so the bounded waits run out; the call
