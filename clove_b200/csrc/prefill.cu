@@ -15,7 +15,6 @@
 // causal mask, RoPE on q and k, scale 1/sqrt(head_dim)) with the exact
 // exponential in place of its polynomial approximation (lazy.rs:4846-4851).
 #include <algorithm>
-#include <cstdlib>
 #include <cmath>
 
 #include "../../include/clove_cuda.h"
