@@ -23,6 +23,7 @@ struct PrefillArgs {
   uint32_t wait_limit;
   float qscale;                 // scale * log2(e)
   int inject_stall;             // test hook (tensor-core prefill): one K/V step is never filled
+  unsigned long long* trace;    // step timeline of CTA 0 (trace builds only; null otherwise)
 };
 
 // Work list: every (sequence, tile of p.tq prompt tokens), ordered by key

@@ -482,7 +482,7 @@ int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, co
       (pool.head_dim != 64 && pool.head_dim != 128))
     return CLOVE_ERR_UNSUPPORTED;
   unsigned char* w = static_cast<unsigned char*>(ws);
-  PrefillArgs a;
+  PrefillArgs a{};
   a.q = q_rot;
   a.out = out;
   a.cu_seqlens = cu_seqlens;

@@ -179,8 +179,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the plan kernel's list
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0) a.trace[16 + 16 * 32 * 16 + 2 * blockIdx.x] = gtime();
+  }
   const int n_units = *a.n_items * a.hkv;
 
+  // trace builds: CTA 0's first 16 units, 32 steps each, 16 events per step:
+  // 0-2 softmax A (S landed, S read, P ready), 3-5 softmax B, 6-9 MMA issue
+  // of S_A, P_B.V, S_B, P_A.V; then each CTA's start (past the plan) and end
+  auto mark = [&](int ui, int s, int k) {
+    if constexpr (kTrace) {
+      if (a.trace && blockIdx.x == 0 && ui < 16 && s < 32) a.trace[16 + (ui * 32 + s) * 16 + k] = gtime();
+    }
+  };
   auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
     if (abort_flag) return false;
     if (!mbar_wait_bounded(bar, parity, a.err, a.wait_limit)) {
@@ -341,6 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = (g + s) % kStages;
         if (t == 0 && !wait(&k_full[st], (uint32_t)((g + s) / kStages) & 1u)) return false;
         tc_fence_after();
+        mark(ui, s, 6 + 2 * t);
         const uint32_t qa = smem_u32(sQ + t * kQTile), ka = smem_u32(sKV + (size_t)st * kStage);
 #pragma unroll
         for (int c = 0; c < 2; ++c)
@@ -359,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait(&v_full[st], (uint32_t)((g + s) / kStages) & 1u)) return false;
         if (s == 0 && !wait(&o_empty[t], ((uint32_t)uc[t] & 1u) ^ 1u)) return false;
         tc_fence_after();
+        mark(ui, s, t == 0 ? 9 : 7);
         const uint32_t va = smem_u32(sKV + (size_t)st * kStage + kKV);
 #pragma unroll
         for (int c = 0; c < 2; ++c)
@@ -458,10 +471,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ++sc;
         tc_fence_after();
+        if ((warp & 3) == 0 && lane == 0) mark(ui, s, 3 * t);
         float v[128];
 #pragma unroll
         for (int i = 0; i < 8; ++i) tmem_ld16f_nowait(sreg + 16u * i, v + 16 * i);
         tmem_wait_ld();
+        if ((warp & 3) == 0 && lane == 0) mark(ui, s, 3 * t + 1);
         const int key0 = s * kKeys;
         float mx = -INFINITY;
         if (key0 + kKeys - 1 <= pos) {
@@ -540,6 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
         }
         tc_fence_before();
+        if ((warp & 3) == 0 && lane == 0) mark(ui, s, 3 * t + 2);
         mbar_arrive(&p_full[t]);
         ++pc;
       }
@@ -570,6 +586,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (kTrace) {
+    if (a.trace && threadIdx.x == 0) a.trace[16 + 16 * 32 * 16 + 2 * blockIdx.x + 1] = gtime();
+  }
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
@@ -624,7 +643,7 @@ int launch_prefill_tc(const clove_pool& pool, const void* q_rot, float* out, con
   if (!rc) rc = encode_map(&tm_v, pool.v_cache, pool.dtype, slots, pool.num_kv_heads, 1, pool.block_size);
   if (rc) return rc;
   unsigned char* w = static_cast<unsigned char*>(ws);
-  PrefillArgs a;
+  PrefillArgs a{};
   a.q = q_rot;
   a.out = out;
   a.cu_seqlens = cu_seqlens;
@@ -648,6 +667,7 @@ int launch_prefill_tc(const clove_pool& pool, const void* q_rot, float* out, con
   a.wait_limit = debug_wait_limit();
   a.inject_stall = debug_inject_stall();
   a.qscale = scale * kLog2e;
+  a.trace = kTrace ? trace_buffer() : nullptr;
   prefill_plan_kernel<<<1, 1024, 0, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
