@@ -102,6 +102,9 @@ bool prefill_tc_supported(const clove_pool& pool, int num_q_heads);
 int launch_prefill_tc(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                       const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
                       int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);
+int launch_prefill_tc2(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
+                       const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
+                       int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);
 int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                        const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
                        int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);

@@ -15,6 +15,7 @@
 // causal mask, RoPE on q and k, scale 1/sqrt(head_dim)) with the exact
 // exponential in place of its polynomial approximation (lazy.rs:4846-4851).
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 
 #include "../../include/clove_cuda.h"
@@ -305,7 +306,16 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, co
     // 5th-generation tensor cores where the shape is covered (16-bit pools,
     // head_dim 128, group dividing 128, block_size dividing 128), unless the
     // warp-MMA variant is forced (2)
-    if (decode_variant() == 0 && prefill_tc_supported(*pool, num_q_heads))
+    // The 2-CTA kernel (M = 256 over an SM pair) for prompts averaging 1024
+    // tokens or more; the one-CTA kernel's units of two tiles waste less on
+    // short prompts.  CLOVE_PREFILL_CTAS = 1 or 2 (read per call) forces one.
+    int ctas = 0;
+    if (const char* v = std::getenv("CLOVE_PREFILL_CTAS")) ctas = std::atoi(v);
+    if (ctas != 1 && ctas != 2) ctas = (long long)num_tokens >= 1024LL * batch ? 2 : 1;
+    if (decode_variant() == 0 && prefill_tc_supported(*pool, num_q_heads) && ctas == 2)
+      rc = launch_prefill_tc2(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride, batch,
+                              num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);
+    else if (decode_variant() == 0 && prefill_tc_supported(*pool, num_q_heads))
       rc = launch_prefill_tc(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride, batch,
                              num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);
     if (rc == CLOVE_ERR_UNSUPPORTED)

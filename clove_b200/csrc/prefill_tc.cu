@@ -105,14 +105,6 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       : "memory");
 }
 
-// 2^x with the accuracy P needs (it is rounded to 16 bits next): the
-// special-function unit's approximation, -inf -> +0.
-__device__ __forceinline__ float exp2_sfu(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 template <typename T>
 __device__ __forceinline__ uint32_t pack_pair(float lo, float hi);
 template <>
@@ -478,17 +470,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         if ((warp & 3) == 0 && lane == 0) mark(ui, s, 3 * t + 1);
         const int key0 = s * kKeys;
-        float mx = -INFINITY;
-        if (key0 + kKeys - 1 <= pos) {
+        if (key0 + kKeys - 1 > pos) {  // the causal mask, only on steps that reach past the row's position
 #pragma unroll
-          for (int k = 0; k < 128; ++k) mx = fmaxf(mx, v[k]);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 128; ++k) {
-            v[k] = key0 + k <= pos ? v[k] : -INFINITY;
-            mx = fmaxf(mx, v[k]);
-          }
+          for (int k = 0; k < 128; ++k) v[k] = key0 + k <= pos ? v[k] : -INFINITY;
         }
+        float mx = row_max128(v);
         mx *= a.qscale;  // the row's max, log2 domain (the scale is positive)
         // P is taken relative to a reference m that moves only when the
         // row's max rises by more than 8 (log2 units): P <= 2^8 stays exact
@@ -498,12 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float m_new = move ? mx : m;
         const float ref = m_new == -INFINITY ? 0.f : m_new;
         const float corr = move ? exp2f(m - ref) : 1.f;  // 0 when m was -inf
-        float rs = 0.f;
-#pragma unroll
-        for (int k = 0; k < 128; ++k) {
-          v[k] = exp2_sfu(fmaf(v[k], a.qscale, -ref));
-          rs += v[k];
-        }
+        const float rs = row_exp2_sum128(v, a.qscale, ref);
         l = l * corr + rs;
         const bool rescale = move && s > 0 && m != -INFINITY;
         m = m_new;

@@ -85,4 +85,57 @@ __host__ __device__ inline uint32_t f16_idesc(bool bf16, int m, int n, int b_mn)
          ((uint32_t)(m >> 4) << 24);
 }
 
+// ---- softmax row helpers (one 128-score row per thread) ----
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t x, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(x));
+}
+
+// Max of 128 values: three-input max in 8 independent chains.
+__device__ __forceinline__ float row_max128(const float (&v)[128]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = max3f(v[i], v[8 + i], v[16 + i]);
+#pragma unroll
+  for (int k = 24; k < 120; k += 16)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = max3f(m[i], v[k + i], v[k + 8 + i]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], v[120 + i]);
+  return max3f(max3f(m[0], m[1], m[2]), max3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
+// v[k] <- 2^(v[k] * scale - ref) (the special-function unit's 2^x, -inf ->
+// +0); returns the sum.  Scale-and-shift and the sum run as packed f32x2
+// operations, two elements per instruction.
+__device__ __forceinline__ float row_exp2_sum128(float (&v)[128], float scale, float ref) {
+  const uint64_t sc = pack_f32x2(scale, scale), nr = pack_f32x2(-ref, -ref);
+  uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int k = 0; k < 128; k += 2) {
+    uint64_t x = pack_f32x2(v[k], v[k + 1]);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(x) : "l"(x), "l"(sc), "l"(nr));
+    float x0, x1;
+    unpack_f32x2(x, x0, x1);
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v[k]) : "f"(x0));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v[k + 1]) : "f"(x1));
+    const uint64_t y = pack_f32x2(v[k], v[k + 1]);
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(acc[(k >> 1) & 3]) : "l"(acc[(k >> 1) & 3]), "l"(y));
+  }
+  float s[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) unpack_f32x2(acc[i], s[2 * i], s[2 * i + 1]);
+  return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
+}
+
 }  // namespace clove

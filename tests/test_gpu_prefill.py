@@ -99,7 +99,7 @@ def test_prefill_matches_oracle(dtype, hq, hkv, d, bs, theta, variant):
 
 
 def test_prefill_long_prompt_multi_chunk():
-    # one 3000-token prompt: its late tokens attend over many chunks (split-K path)
+    # one 3000-token prompt (the 2-CTA kernel): its late tokens attend over many 128-key steps
     import oracle
     from clove_b200 import KVPool
     c = _case(torch.bfloat16, 8, 1, 128, 32, prior=[0], prompt=[3000], seed=9)
@@ -162,6 +162,7 @@ def _prefill_vs_oracle(dtype, hq, hkv, d, bs, theta, prior, prompt, seed, varian
     return out
 
 
+@pytest.mark.parametrize("ctas", ["1", "2"])  # the one-CTA kernel and the 2-CTA (SM pair) kernel
 @pytest.mark.parametrize("dtype,hq,hkv,bs,theta", [
     (torch.bfloat16, 8, 2, 32, 10000.0),   # group 4
     (torch.bfloat16, 16, 2, 16, 0.0),      # group 8
@@ -169,27 +170,32 @@ def _prefill_vs_oracle(dtype, hq, hkv, d, bs, theta, prior, prompt, seed, varian
     (torch.bfloat16, 4, 4, 8, 10000.0),    # group 1
     (torch.float16, 4, 2, 128, 0.0),       # group 2, one block per key step
 ])
-def test_prefill_tensor_core_multi_step(dtype, hq, hkv, bs, theta):
+def test_prefill_tensor_core_multi_step(dtype, hq, hkv, bs, theta, ctas, monkeypatch):
     # contexts and prompts spanning several 128-key steps, prompt tails
     # shorter than a query tile, and a prompt continuing a cached context
+    monkeypatch.setenv("CLOVE_PREFILL_CTAS", ctas)
     _prefill_vs_oracle(dtype, hq, hkv, 128, bs, theta, prior=[300, 0, 129, 7], prompt=[200, 257, 1, 95], seed=hq + bs)
 
 
-def test_prefill_tensor_core_matches_warp_mma():
-    # the tcgen05 kernel and the warp-MMA kernel agree (both against the oracle)
+@pytest.mark.parametrize("ctas", ["1", "2"])
+def test_prefill_tensor_core_matches_warp_mma(ctas, monkeypatch):
+    # the tcgen05 kernels and the warp-MMA kernel agree (both against the oracle)
+    monkeypatch.setenv("CLOVE_PREFILL_CTAS", ctas)
     a = _prefill_vs_oracle(torch.bfloat16, 16, 4, 128, 32, 10000.0, prior=[50, 0], prompt=[400, 130], seed=3)
     b = _prefill_vs_oracle(torch.bfloat16, 16, 4, 128, 32, 10000.0, prior=[50, 0], prompt=[400, 130], seed=3,
                            variant="mma")
     assert torch.isfinite(a).all() and torch.isfinite(b).all()
 
 
-def test_prefill_tensor_core_stuck_wait_times_out():
+@pytest.mark.parametrize("ctas", ["1", "2"])
+def test_prefill_tensor_core_stuck_wait_times_out(ctas, monkeypatch):
     # failure detection without a GPU fault: one K/V step is never filled, the
     # bounded waits run out, the call completes with CLOVE_FLAG_TIMEOUT in the
     # pool's status word, and the next call on the same context is correct
     import time
 
     from clove_b200 import KVPool, _lib
+    monkeypatch.setenv("CLOVE_PREFILL_CTAS", ctas)
     L = _lib.lib()
     c = _case(torch.bfloat16, 8, 2, 128, 32, prior=[0, 100], prompt=[300, 60], seed=5)
     pool = KVPool(c["nb"], 32, 2, 128, torch.bfloat16, 0)
