@@ -59,7 +59,7 @@ constexpr uint32_t kSmem = 2 * kQTile + kStages * kStage + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // + 128 tile
 constexpr uint32_t kTmemO = 256;  // + 128 tile
-constexpr int kRemoteArrivals = 2 * kTileThreads;  // both CTAs' softmax threads of a tile
+constexpr int kRemoteArrivals = 2 * kTileThreads / 32;  // one per softmax warp of a tile, both CTAs
 
 struct QuadUnit {
   int u, b, jq, h, valid;  // u: the claimed unit index
@@ -267,10 +267,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
   // trace builds: CTA 0's first 16 units, 32 steps each, 16 events per step
   // (0-2 softmax A: S landed, S read, P ready; 3-5 softmax B; 6-9 MMA issue
-  // of S_A, P_B.V, S_B, P_A.V); then each CTA's start and end
+  // of S_A, P_B.V, S_B, P_A.V; 10-15 the peer's softmax events); then each
+  // CTA's start and end
   auto mark = [&](int ui, int s, int k) {
     if constexpr (kTrace) {
-      if (a.trace && blockIdx.x == 0 && ui < 16 && s < 32) a.trace[16 + (ui * 32 + s) * 16 + k] = gtime();
+      if (a.trace && blockIdx.x < 2 && ui < 16 && s < 32 && (blockIdx.x == 0 || k < 6))
+        a.trace[16 + (ui * 32 + s) * 16 + k + (blockIdx.x == 1 ? 10 : 0)] = gtime();
     }
   };
   auto unit_of = [&](int u) {
@@ -646,7 +648,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         if ((warp & 3) == 0 && lane == 0) mark(ui, s, 3 * t + 2);
-        arrive_remote(lead_p_full);
+        // each lane's P stores (and V zeroing) are fenced above; the warp
+        // meets, then one lane arrives for it
+        __syncwarp();
+        if (lane == 0) arrive_remote(lead_p_full);
         ++pc;
       }
       if (!ok) break;
@@ -667,7 +672,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
         tc_fence_before();
-        arrive_remote(lead_o_empty);
+        __syncwarp();
+        if (lane == 0) arrive_remote(lead_o_empty);
       }
       g += ns_all;
       ++ui;
