@@ -98,13 +98,18 @@ cudaError_t launch_dependent(Kern kern, unsigned grid, unsigned threads, size_t 
 }
 
 size_t prefill_mma_scratch_bytes(int num_tokens);
+// What a tensor-core prefill launch issues: its plan kernel (the work list),
+// the attention kernel (a programmatic dependent of the kernel before it), or both.
+constexpr int kPrefillPlanOnly = 1, kPrefillKernelOnly = 2, kPrefillBoth = 3;
 bool prefill_tc_supported(const clove_pool& pool, int num_q_heads);
 int launch_prefill_tc(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                       const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
-                      int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);
+                      int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream,
+                      int phase);
 int launch_prefill_tc2(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                        const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
-                       int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);
+                       int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream,
+                      int phase);
 int launch_prefill_mma(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                        const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
                        int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream);

@@ -129,23 +129,25 @@ __global__ void __launch_bounds__(128) prefill_prep_kernel(const PrefillPrepArgs
       qd[u] = rot ? rope8<T>(x, cs, sn, (u % vpr) * (EPV / 2)) : x;
     }
   }
-  if (!in_range) return;
   // K (rotated) and V into the slot
-  const int phys = __ldg(bt + pos / p.bs);
-  if (phys < 0 || phys >= p.num_blocks) {
-    if (threadIdx.x == 0) atomicOr(p.flags, CLOVE_FLAG_BLOCK_OOB);
-    return;
+  const int phys = in_range ? __ldg(bt + pos / p.bs) : -1;
+  if (in_range && (phys < 0 || phys >= p.num_blocks) && threadIdx.x == 0) atomicOr(p.flags, CLOVE_FLAG_BLOCK_OOB);
+  if (in_range && phys >= 0 && phys < p.num_blocks) {
+    const size_t row = ((size_t)phys * p.bs + pos % p.bs) * p.hkv * p.D;
+    const uint4* ks = reinterpret_cast<const uint4*>(static_cast<const T*>(p.k) + (size_t)t * p.hkv * p.D);
+    const uint4* vs = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v) + (size_t)t * p.hkv * p.D);
+    uint4* kc = reinterpret_cast<uint4*>(static_cast<T*>(p.k_cache) + row);
+    uint4* vc = reinterpret_cast<uint4*>(static_cast<T*>(p.v_cache) + row);
+    for (int u = threadIdx.x; u < p.hkv * vpr; u += blockDim.x) {
+      const uint4 x = __ldg(ks + u);
+      kc[u] = rot ? rope8<T>(x, cs, sn, (u % vpr) * (EPV / 2)) : x;
+      vc[u] = __ldg(vs + u);
+    }
   }
-  const size_t row = ((size_t)phys * p.bs + pos % p.bs) * p.hkv * p.D;
-  const uint4* ks = reinterpret_cast<const uint4*>(static_cast<const T*>(p.k) + (size_t)t * p.hkv * p.D);
-  const uint4* vs = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v) + (size_t)t * p.hkv * p.D);
-  uint4* kc = reinterpret_cast<uint4*>(static_cast<T*>(p.k_cache) + row);
-  uint4* vc = reinterpret_cast<uint4*>(static_cast<T*>(p.v_cache) + row);
-  for (int u = threadIdx.x; u < p.hkv * vpr; u += blockDim.x) {
-    const uint4 x = __ldg(ks + u);
-    kc[u] = rot ? rope8<T>(x, cs, sn, (u % vpr) * (EPV / 2)) : x;
-    vc[u] = __ldg(vs + u);
-  }
+  // Launched as a programmatic dependent of the tensor-core path's plan
+  // kernel (which it does not read): wait for it here, at the end, so that
+  // this grid's completion implies the plan's for the kernel after it.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // f32 pools: the same with element-wise rotation.
@@ -282,12 +284,45 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, co
                         (pool->head_dim == 64 || pool->head_dim == 128);
   p.write_rows = (tc_path || mma_path) ? 0 : 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (pool->dtype) {
-    case CLOVE_DTYPE_F32: prefill_prep_f32_kernel<<<num_tokens, 128, 0, s>>>(p); break;
-    case CLOVE_DTYPE_BF16: prefill_prep_kernel<__nv_bfloat16><<<num_tokens, 128, 0, s>>>(p); break;
-    default: prefill_prep_kernel<__half><<<num_tokens, 128, 0, s>>>(p); break;
+  // The 2-CTA kernel (M = 256 over an SM pair) for prompts averaging 1024
+  // tokens or more; the one-CTA kernel's units of two tiles waste less on
+  // short prompts.  CLOVE_PREFILL_CTAS = 1 or 2 (read per call) forces one.
+  int ctas = 0;
+  if (const char* v = std::getenv("CLOVE_PREFILL_CTAS")) ctas = std::atoi(v);
+  if (ctas != 1 && ctas != 2) ctas = (long long)num_tokens >= 1024LL * batch ? 2 : 1;
+  cudaError_t e = cudaSuccess;
+  if (tc_path) {
+    // the tensor-core path's work list first (it reads only the lengths),
+    // then the prep kernel as its programmatic dependent, so the two overlap
+    const int rc = ctas == 2 ? launch_prefill_tc2(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables,
+                                                  bt_stride, batch, num_tokens, num_q_heads, scale, max_ctx,
+                                                  ws + L.off_decode, s, kPrefillPlanOnly)
+                             : launch_prefill_tc(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables,
+                                                 bt_stride, batch, num_tokens, num_q_heads, scale, max_ctx,
+                                                 ws + L.off_decode, s, kPrefillPlanOnly);
+    if (rc != CLOVE_OK) {
+      if (prev >= 0 && prev != pool->device) cudaSetDevice(prev);
+      return rc;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)num_tokens);
+    cfg.blockDim = dim3(128);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = pool->dtype == CLOVE_DTYPE_BF16 ? cudaLaunchKernelEx(&cfg, prefill_prep_kernel<__nv_bfloat16>, p)
+                                        : cudaLaunchKernelEx(&cfg, prefill_prep_kernel<__half>, p);
+  } else {
+    switch (pool->dtype) {
+      case CLOVE_DTYPE_F32: prefill_prep_f32_kernel<<<num_tokens, 128, 0, s>>>(p); break;
+      case CLOVE_DTYPE_BF16: prefill_prep_kernel<__nv_bfloat16><<<num_tokens, 128, 0, s>>>(p); break;
+      default: prefill_prep_kernel<__half><<<num_tokens, 128, 0, s>>>(p); break;
+    }
+    e = cudaGetLastError();
   }
-  cudaError_t e = cudaGetLastError();
   if (prev >= 0 && prev != pool->device) cudaSetDevice(prev);
   if (e != cudaSuccess) {
     set_last_error("paged_prefill prep launch: %s", cudaGetErrorString(e));
@@ -306,18 +341,12 @@ int clove_cuda_paged_prefill(clove_pool_t pool, const void* q, const void* k, co
     // 5th-generation tensor cores where the shape is covered (16-bit pools,
     // head_dim 128, group dividing 128, block_size dividing 128), unless the
     // warp-MMA variant is forced (2)
-    // The 2-CTA kernel (M = 256 over an SM pair) for prompts averaging 1024
-    // tokens or more; the one-CTA kernel's units of two tiles waste less on
-    // short prompts.  CLOVE_PREFILL_CTAS = 1 or 2 (read per call) forces one.
-    int ctas = 0;
-    if (const char* v = std::getenv("CLOVE_PREFILL_CTAS")) ctas = std::atoi(v);
-    if (ctas != 1 && ctas != 2) ctas = (long long)num_tokens >= 1024LL * batch ? 2 : 1;
-    if (decode_variant() == 0 && prefill_tc_supported(*pool, num_q_heads) && ctas == 2)
+    if (tc_path && ctas == 2)
       rc = launch_prefill_tc2(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride, batch,
-                              num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);
-    else if (decode_variant() == 0 && prefill_tc_supported(*pool, num_q_heads))
+                              num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s, kPrefillKernelOnly);
+    else if (tc_path)
       rc = launch_prefill_tc(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride, batch,
-                             num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);
+                             num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s, kPrefillKernelOnly);
     if (rc == CLOVE_ERR_UNSUPPORTED)
       rc = launch_prefill_mma(*pool, ws + L.off_q, out, cu_seqlens, context_lens, block_tables, bt_stride, batch,
                               num_tokens, num_q_heads, scale, max_ctx, ws + L.off_decode, s);

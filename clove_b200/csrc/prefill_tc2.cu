@@ -236,7 +236,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers are initialised before anyone arrives remotely
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // the plan kernel's list
+  // the previous kernel (the prep kernel, which itself waited for the plan
+  // kernel) has finished: the cache rows, rotated q and the work list are in place
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if constexpr (kTrace) {
     if (a.trace && threadIdx.x == 0) a.trace[16 + 16 * 32 * 16 + 2 * blockIdx.x] = gtime();
   }
@@ -722,7 +724,7 @@ static int encode_map(CUtensorMap* map, const void* base, int dtype, long long t
 // arguments and shape coverage as launch_prefill_tc.
 int launch_prefill_tc2(const clove_pool& pool, const void* q_rot, float* out, const int32_t* cu_seqlens,
                        const int32_t* context_lens, const int32_t* block_tables, int bt_stride, int batch,
-                       int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream) {
+                       int num_tokens, int num_q_heads, float scale, int max_ctx, void* ws, cudaStream_t stream, int phase) {
   const int group = num_q_heads / pool.num_kv_heads;
   const int tq = kRows / group;
   CUtensorMap tm_q, tm_k, tm_v;
@@ -758,13 +760,17 @@ int launch_prefill_tc2(const clove_pool& pool, const void* q_rot, float* out, co
   a.inject_stall = debug_inject_stall();
   a.qscale = scale * kLog2e;
   a.trace = kTrace ? trace_buffer() : nullptr;
-  prefill_plan_kernel<<<1, 1024, 0, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    set_last_error("prefill plan launch: %s", cudaGetErrorString(e));
-    return CLOVE_ERR_CUDA;
+  cudaError_t e = cudaSuccess;
+  if (phase & kPrefillPlanOnly) {
+    prefill_plan_kernel<<<1, 1024, 0, stream>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      set_last_error("prefill plan launch: %s", cudaGetErrorString(e));
+      return CLOVE_ERR_CUDA;
+    }
+    count_launches(1);
   }
-  count_launches(1);
+  if (!(phase & kPrefillKernelOnly)) return CLOVE_OK;
   const bool bf16 = pool.dtype == CLOVE_DTYPE_BF16;
   auto kern = bf16 ? prefill_tc2_kernel<__nv_bfloat16> : prefill_tc2_kernel<__half>;
   static std::once_flag attr_once[2];
