@@ -143,6 +143,12 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return pol;
 }
 
+// Fetch a tensor map (a __grid_constant__ kernel parameter) into the
+// descriptor cache ahead of its first bulk tensor copy.
+__device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 // 3-D tiled bulk tensor load global -> shared, completion counted on `bar`.
 // Coordinates are in elements, innermost first.  c0 is always 0 here (a tile
 // starts at the beginning of a head row), which satisfies the 16-byte rule

@@ -221,6 +221,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     const uint64_t pol = policy_evict_first();
+    if (lane == 0) {
+      prefetch_tensor_map(&tm_q);
+      prefetch_tensor_map(&tm_k);
+      prefetch_tensor_map(&tm_v);
+    }
     const int bs = a.bs, bps = kKeys / bs;  // blocks per step
     int ui = 0, g = 0, stalled_g = -1;
     bool ok = true;

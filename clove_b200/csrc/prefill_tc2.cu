@@ -307,6 +307,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
     const uint64_t pol = policy_evict_first();
+    if (lane == 0) {
+      prefetch_tensor_map(&tm_q);
+      prefetch_tensor_map(&tm_k);
+      prefetch_tensor_map(&tm_v);
+    }
     const int bs = a.bs, bps = kKeys / bs;
     int ui = 0, g = 0;
     bool ok = true;

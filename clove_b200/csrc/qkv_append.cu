@@ -315,6 +315,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1)
       // requested before griddepcontrol.wait; x, which the previous kernel
       // may write, only after it.
       const bool stall = a.inject_stall && blockIdx.x == 0;
+      prefetch_tensor_map(&tm_x);  // x is copied right after griddepcontrol.wait
       const int n = (int)(u_end - u_begin);
       const int pre = min(n, a.nstage);
       auto load_w = [&](int i) {
@@ -596,6 +597,7 @@ __global__ void __launch_bounds__(kClusterThreads, 1)
       // griddepcontrol.wait (the packed weights are never written by the
       // kernel this one may overlap), x only after it
       const bool stall = a.inject_stall && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+      prefetch_tensor_map(&tm_x);  // x is copied right after griddepcontrol.wait
       const int pre = min(nkb, a.nstage);
       const unsigned char* w = static_cast<const unsigned char*>(a.w_packed);
       auto load_w = [&](int i) {
