@@ -300,16 +300,27 @@ __device__ void combine_segment(const DecodeArgs& a, int b, int h, const int* pi
       }
     }
     __syncthreads();
-    for (int o = o_begin + tid; o < o_end; o += kCombineThreads) {
-      const int g = o / (D / 4), d4 = o - g * (D / 4);
+    // Output float4s [o_begin, o_end): kpar threads (lanes of one warp) per
+    // output, each summing every kpar-th piece, then a shuffle reduction, so
+    // a small slice over many pieces is not one long chain of loads.
+    const int nout = o_end - o_begin;
+    int kpar = 1;
+    while (kpar < 32 && 2 * kpar * nout <= kCombineThreads) kpar *= 2;
+    const int sub = tid & (kpar - 1);
+    // every lane runs the same number of rounds (the shuffles below are
+    // warp-wide); lanes past the slice carry zeros and store nothing
+    for (int o0 = o_begin; o0 < o_end; o0 += kCombineThreads / kpar) {
+      const int o = o0 + tid / kpar;
+      const bool live = o < o_end;
+      const int g = live ? o / (D / 4) : 0, d4 = live ? o - g * (D / 4) : 0;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (!first) {
+      if (live && !first && sub == 0) {
         const float r = rowR[g];
         const float4 v = reinterpret_cast<const float4*>(run + g * S)[d4];
         acc = make_float4(v.x * r, v.y * r, v.z * r, v.w * r);
       }
-#pragma unroll 8
-      for (int i = 0; i < n; ++i) {
+#pragma unroll 4
+      for (int i = sub; live && i < n; i += kpar) {
         const float w = pm[i * group + g];
         const float4 v = __ldcg(reinterpret_cast<const float4*>(a.partials + ((size_t)pieces[base + i] * group + g) * S) + d4);
         acc.x = fmaf(w, v.x, acc.x);
@@ -317,6 +328,13 @@ __device__ void combine_segment(const DecodeArgs& a, int b, int h, const int* pi
         acc.z = fmaf(w, v.z, acc.z);
         acc.w = fmaf(w, v.w, acc.w);
       }
+      for (int off = kpar / 2; off > 0; off >>= 1) {
+        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off, kpar);
+        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off, kpar);
+        acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off, kpar);
+        acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off, kpar);
+      }
+      if (!live || sub != 0) continue;
       if (last) {
         const float inv = 1.f / rowL[g];
         float* dst = a.out + ((size_t)b * Hq + (size_t)h * group + g) * D + 4 * d4;
