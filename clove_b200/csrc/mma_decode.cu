@@ -20,6 +20,7 @@
 // Pipeline, work units, ring-slot ownership and the epilogue are those of
 // the CUDA-core kernel (decode_common.cuh).
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -348,8 +349,13 @@ int run_mma(const clove_pool& pool, DecodeArgs& a, cudaStream_t stream) {
     set_last_error("paged_decode: tensor-core kernel needs a 16-bit pool, block_size >= 8, group <= 8");
     return CLOVE_ERR_UNSUPPORTED;
   }
-  if (a.group <= 4) return run_mma_cfg<T, D, 3>(pool, a, stream, 96 * 1024, 1);
-  return run_mma_cfg<T, D, 4>(pool, a, stream, 64 * 1024, 2);
+  // CLOVE_DECODE_RING_KB overrides the ring target (a tuning override, read once)
+  static const int ring_kb = [] {
+    const char* v = std::getenv("CLOVE_DECODE_RING_KB");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (a.group <= 4) return run_mma_cfg<T, D, 3>(pool, a, stream, (ring_kb > 0 ? ring_kb : 96) * 1024, 1);
+  return run_mma_cfg<T, D, 4>(pool, a, stream, (ring_kb > 0 ? ring_kb : 64) * 1024, 2);
 }
 
 template int run_mma<__nv_bfloat16, 64>(const clove_pool&, DecodeArgs&, cudaStream_t);
