@@ -229,8 +229,18 @@ def run_reference(args) -> None:
                               "d2h_bytes_per_step": 0}}), flush=True)
 
 
+def _head_gather() -> str:
+    """Output exchange of the c4 KV-head split: "nccl" (all_gather_into_tensor,
+    default: the faster whole step at 2 GPUs) or "peer" (the library's P2P
+    store kernel over NVLink); CLOVE_HEAD_GATHER selects."""
+    g = os.environ.get("CLOVE_HEAD_GATHER", "nccl")
+    if g not in ("peer", "nccl"):
+        raise ValueError(f"CLOVE_HEAD_GATHER={g!r}: expected peer or nccl")
+    return g
+
+
 def _partition(mode: str, name: str, ws: int) -> str:
-    return {"heads": f"kv-heads/{ws} + NCCL all-gather of outputs",
+    return {"heads": f"kv-heads/{ws} + all-gather of outputs ({_head_gather()})",
             "sequences": (f"sequences sharded over {ws} GPUs ({_policy(name)}), own pool per GPU, no collective")
             if ws > 1 else "1 GPU",
             "replica": f"{ws} independent full replicas"}[mode]
@@ -304,6 +314,9 @@ class DecodeCase:
             hl = spec.num_q_heads // ws
             q = q_all[:, rank * hl:(rank + 1) * hl].contiguous()  # this rank's query heads
             self.gbuf = torch.empty((ws * lay.batch, hl, spec.head_dim), dtype=torch.float32, device=dev)
+            if _head_gather() == "peer":
+                from clove_b200.distributed import PeerGather
+                self.peer = PeerGather(lay.batch * hl * spec.head_dim * 4, dev)
             self.global_batch = lay.batch
             self.kv_local = lay.kv_bytes() // ws
             self.kv_total = lay.kv_bytes()
@@ -325,13 +338,18 @@ class DecodeCase:
         self.out = torch.empty((lay.batch, q.shape[1], spec.head_dim), dtype=torch.float32, device=dev)
         self.max_ctx = lay.max_ctx
         self._hs = head_sharded_append_decode
+        if not hasattr(self, "peer"):
+            self.peer = None
 
     def decode(self):
         return self.pool.append_decode(self.q, self.kn, self.vn, self.bt, self.cl, max_ctx=self.max_ctx, out=self.out)
 
     def gather(self):
         import torch.distributed as dist
-        dist.all_gather_into_tensor(self.gbuf, self.out)
+        if self.peer is not None:
+            self.peer(self.out, self.gbuf)
+        else:
+            dist.all_gather_into_tensor(self.gbuf, self.out)
 
     def step(self):
         self.decode()
@@ -339,6 +357,8 @@ class DecodeCase:
             self.gather()
 
     def close(self):
+        if self.peer is not None:
+            self.peer.close()
         self.pool.close()
 
 
@@ -494,7 +514,8 @@ def run_ours(args) -> None:
         def e2e_step():
             for d, h in ((dq, hq), (dk, hk), (dv, hv), (dbt, hbt), (dcl, hcl)):
                 d.copy_(h, non_blocking=True)
-            res = case._hs(case.pool, dq, dk, dv, dbt, dcl, ws, case.max_ctx, out_local=out, gather_buf=case.gbuf)
+            res = case._hs(case.pool, dq, dk, dv, dbt, dcl, ws, case.max_ctx, out_local=out, gather_buf=case.gbuf,
+                           peer=case.peer)
             hout.copy_(res, non_blocking=True)
     else:
         # Through the reference-facing FFI (include/clove_ffi.h): tensors made

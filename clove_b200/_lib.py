@@ -24,6 +24,8 @@ FLAG_CTX_RANGE = 2
 FLAG_SLOT_OOB = 4
 FLAG_TIMEOUT = 8
 
+IPC_HANDLE_BYTES = 64
+
 DTYPE_F32 = 0
 DTYPE_F16 = 16
 DTYPE_BF16 = 160
@@ -56,6 +58,13 @@ SIGNATURES = {
                                             _sz, _vp]),
     "clove_cuda_paged_append_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _i, _vp, _i, _f, _i, _vp, _vp]),
     "clove_cuda_noalloc_status": (_i, [_i, _vp, _ip]),
+    "clove_cuda_peer_gather_buffer_bytes": (_sz, [_sz, _i]),
+    "clove_cuda_peer_buffer_alloc": (_i, [_i, _sz, C.POINTER(_vp), _vp]),
+    "clove_cuda_peer_buffer_open": (_i, [_i, _vp, C.POINTER(_vp)]),
+    "clove_cuda_peer_buffer_close": (_i, [_vp]),
+    "clove_cuda_peer_buffer_free": (_i, [_vp]),
+    "clove_cuda_peer_gather": (_i, [_vp, _sz, _vp, _i, _i, _vp, _vp]),
+    "clove_cuda_peer_gather_status": (_i, [_vp, _sz, _i, _vp, _ip]),
     "clove_cuda_prefill_workspace_size": (_sz, [_vp, _i, _i, _i, _i]),
     "clove_cuda_paged_prefill": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _f, _f, _i, _vp, _vp, _sz,
                                       _vp]),

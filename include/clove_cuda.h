@@ -260,6 +260,46 @@ int clove_cuda_paged_append_decode_noalloc(clove_pool_t pool, const void* q,
                                            int batch, float scale, int max_ctx,
                                            float* out, void* stream);
 
+/* ---- output exchange over NVLink peer memory (KV-head split) ---------- */
+/* The reference assembles per-shard results through host memory
+ * (MultiGPUOrchestrator::synchronize_gradients, src/distributed.rs:204-300);
+ * these replace that step for the head-split decode with P2P stores between
+ * the ranks' GPUs.  One process per GPU; every rank allocates a receive
+ * buffer, publishes its IPC handle (e.g. through torch.distributed), opens
+ * the peers' handles and keeps a device array of the world's buffer
+ * pointers (its own at index rank). */
+#define CLOVE_IPC_HANDLE_BYTES 64
+
+/* Receive-buffer bytes for slices of `slice_bytes` over `world` ranks. */
+size_t clove_cuda_peer_gather_buffer_bytes(size_t slice_bytes, int world);
+
+/* cudaMalloc `bytes` on `device`, zero them and write the allocation's IPC
+ * handle (CLOVE_IPC_HANDLE_BYTES) to `ipc_handle`. */
+int clove_cuda_peer_buffer_alloc(int device, size_t bytes, void** ptr, void* ipc_handle);
+/* Map a peer's buffer from its IPC handle into this process (on `device`). */
+int clove_cuda_peer_buffer_open(int device, const void* ipc_handle, void** ptr);
+/* Unmap a buffer from clove_cuda_peer_buffer_open. */
+int clove_cuda_peer_buffer_close(void* ptr);
+/* Free a buffer from clove_cuda_peer_buffer_alloc (after the peers closed it). */
+int clove_cuda_peer_buffer_free(void* ptr);
+
+/* All-gather of equal slices: out[r * slice_bytes ...] receives rank r's
+ * `src` on every rank (the layout of an all-gather into one tensor).
+ * peer_bufs: device array of `world` receive-buffer pointers as mapped in
+ * this process.  Every rank must make the same sequence of calls with the
+ * same slice_bytes; the kernel waits (bounded) for the peers' slices, so the
+ * ranks' calls must be able to run at the same time (one GPU per rank).
+ * slice_bytes, src and out: multiples of 16 bytes.  Capturable in a CUDA
+ * graph.  A wait that runs out sets CLOVE_FLAG_TIMEOUT (read it with
+ * clove_cuda_peer_gather_status) and leaves that peer's part of `out`
+ * undefined. */
+int clove_cuda_peer_gather(const void* src, size_t slice_bytes, void* const* peer_bufs, int rank,
+                           int world, void* out, void* stream);
+/* Synchronise `stream`, read and clear the flags of this rank's receive
+ * buffer; CLOVE_ERR_DEVICE_CHECK if any was set. */
+int clove_cuda_peer_gather_status(void* own_buf, size_t slice_bytes, int world, void* stream,
+                                  int* flags);
+
 /* Check flags (CLOVE_FLAG_*) of the most recent
  * clove_cuda_paged_append_decode_noalloc call on `device`: synchronises
  * `stream`, reads and clears the flag word of the built-in scratch, like
@@ -285,8 +325,9 @@ uint64_t clove_cuda_launch_count(void);
 
 /* Testing hook (failure detection without a GPU fault).  wait_limit: polls
  * after which a pipeline wait gives up (0 = the default, seconds of wall
- * time); inject_stall = 1 makes producers skip one stage's copy (decode:
- * the first stage of every CTA's first piece; fused projection: the first
+ * time; a peer-gather receive gives up after wait_limit x 64 ns);
+ * inject_stall = 1 makes producers skip one stage's copy (decode: the first
+ * stage of every CTA's first piece; fused projection: the first
  * stage of the first CTA), so the consumers' bounded waits run out: the call
  * then completes, reports CLOVE_FLAG_TIMEOUT through clove_cuda_decode_status
  * (the pool's status for the projection), and its output is undefined.

@@ -51,6 +51,13 @@ unsafe extern "C" {
     pub fn clove_cuda_qkv_append(pool: CPool, x: *mut c_void, w_packed: *mut c_void, bias: *mut c_float, batch: c_int, hidden: c_int, num_q_heads: c_int, block_tables: *mut i32, bt_stride: c_int, context_lens: *mut i32, rope_theta: c_float, q_out: *mut c_void, context_lens_out: *mut i32, workspace: *mut c_void, workspace_bytes: usize, stream: *mut c_void) -> c_int;
     pub fn clove_cuda_paged_append_decode_noalloc(pool: CPool, q: *mut c_void, k_new: *mut c_void, v_new: *mut c_void, num_q_heads: c_int, block_tables: *mut i32, bt_stride: c_int, context_lens: *mut i32, batch: c_int, scale: c_float, max_ctx: c_int, out: *mut c_float, stream: *mut c_void) -> c_int;
     pub fn clove_cuda_noalloc_status(device: c_int, stream: *mut c_void, flags: *mut c_int) -> c_int;
+    pub fn clove_cuda_peer_gather_buffer_bytes(slice_bytes: usize, world: c_int) -> usize;
+    pub fn clove_cuda_peer_buffer_alloc(device: c_int, bytes: usize, ptr: *mut *mut c_void, ipc_handle: *mut c_void) -> c_int;
+    pub fn clove_cuda_peer_buffer_open(device: c_int, ipc_handle: *const c_void, ptr: *mut *mut c_void) -> c_int;
+    pub fn clove_cuda_peer_buffer_close(ptr: *mut c_void) -> c_int;
+    pub fn clove_cuda_peer_buffer_free(ptr: *mut c_void) -> c_int;
+    pub fn clove_cuda_peer_gather(src: *const c_void, slice_bytes: usize, peer_bufs: *const *mut c_void, rank: c_int, world: c_int, out: *mut c_void, stream: *mut c_void) -> c_int;
+    pub fn clove_cuda_peer_gather_status(own_buf: *mut c_void, slice_bytes: usize, world: c_int, stream: *mut c_void, flags: *mut c_int) -> c_int;
     pub fn clove_cuda_decode_status(workspace: *mut c_void, stream: *mut c_void, flags: *mut c_int) -> c_int;
     pub fn clove_cuda_set_decode_variant(variant: c_int) -> c_int;
     pub fn clove_cuda_launch_count() -> u64;
