@@ -59,11 +59,6 @@ struct GatherArgs {
   uint64_t wait_ns;   // how long a receive waits before it gives up
 };
 
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -111,13 +106,13 @@ __global__ void __launch_bounds__(kGatherThreads) peer_gather_kernel(GatherArgs 
       const uint32_t* cnt = reinterpret_cast<const uint32_t*>(own + a.count_off) + p;
       const uint32_t target = call * (uint32_t)a.chunks;
       int got = 0;
-      const uint64_t t0 = global_ns();
+      const uint64_t t0 = gtime();
       for (;;) {
         if ((int32_t)(ld_acquire_sys(cnt) - target) >= 0) {
           got = 1;
           break;
         }
-        if (global_ns() - t0 > a.wait_ns) break;
+        if (gtime() - t0 > a.wait_ns) break;
         __nanosleep(64);
       }
       if (!got) atomicOr(reinterpret_cast<int*>(state + 2), CLOVE_FLAG_TIMEOUT);
