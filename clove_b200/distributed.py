@@ -143,7 +143,9 @@ class PeerGather:
         return out
 
     def status(self, stream=None) -> int:
-        """Flags (CLOVE_FLAG_*) raised by calls since the last status read."""
+        """Flags (CLOVE_FLAG_*) raised by calls since the last status read.
+        After CLOVE_FLAG_TIMEOUT the ranks' counts are out of step: close this
+        gather on every rank and make a new one."""
         flags = C.c_int(0)
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         rc = self._lib.clove_cuda_peer_gather_status(self._own, self.slice_bytes, self.world, s.cuda_stream,

@@ -292,7 +292,8 @@ int clove_cuda_peer_buffer_free(void* ptr);
  * slice_bytes, src and out: multiples of 16 bytes.  Capturable in a CUDA
  * graph.  A wait that runs out sets CLOVE_FLAG_TIMEOUT (read it with
  * clove_cuda_peer_gather_status) and leaves that peer's part of `out`
- * undefined. */
+ * undefined; the ranks' delivery counts are then out of step, so every rank
+ * must replace its receive buffer before the next call. */
 int clove_cuda_peer_gather(const void* src, size_t slice_bytes, void* const* peer_bufs, int rank,
                            int world, void* out, void* stream);
 /* Synchronise `stream`, read and clear the flags of this rank's receive
